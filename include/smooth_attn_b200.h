@@ -1,0 +1,143 @@
+/*
+ * smooth_attn_b200.h — C ABI of the B200 (sm_100a) smooth-attn hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, sizes and
+ * strides (in ELEMENTS), launches on the given CUDA stream (a cudaStream_t
+ * passed as void*, NULL = legacy default stream), never allocates device
+ * memory, never synchronises, and returns an sa_status (0 = success).
+ * Arguments are validated before anything is launched; a rejected call has
+ * no side effects.  The library is stateless apart from per-device attribute
+ * caches, so calls are thread-safe.
+ *
+ * Each declaration names the reference interface it replaces
+ * (NoSelection/smooth-attn, file:line).
+ */
+#ifndef SMOOTH_ATTN_B200_H
+#define SMOOTH_ATTN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SA_API __attribute__((visibility("default")))
+#else
+#define SA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define SA_OK 0
+#define SA_ERR_ARG (-1)         /* bad size / null pointer / bad family       */
+#define SA_ERR_ALIGN (-2)       /* pointer or stride alignment not supported   */
+#define SA_ERR_UNSUPPORTED (-3) /* dtype / head dim / shape not implemented    */
+#define SA_ERR_LAUNCH (-4)      /* CUDA launch error (cudaGetLastError)        */
+#define SA_ERR_TIMEOUT (-5)     /* a bounded device-side wait gave up          */
+#define SA_ERR_CUDA (-6)        /* other CUDA runtime/driver error             */
+
+/* Element types. */
+#define SA_F32 0
+#define SA_F16 1
+#define SA_BF16 2
+
+/* Library version, (major << 16) | minor. */
+SA_API int sa_version(void);
+
+/* Human-readable text for a status code (static storage). */
+SA_API const char* sa_status_string(int status);
+
+/* Text of the last CUDA error seen by this thread inside the library. */
+SA_API const char* sa_last_cuda_error(void);
+
+/*
+ * Squareplus normalization forward over rows of length `cols`.
+ *   y_j = squareplus(alpha * (x_j - theta))^power,  squareplus(a) = (a + sqrt(a^2+4)) / 2
+ *   out_j = y_j / (sum_j y_j + 1e-12)
+ * causal = 0: every column is visible (row-wise kernel).
+ * causal = 1: rows are the rows of [M, cols, cols] score matrices stacked as
+ *             [M*cols, cols]; row r is query position q = r % cols and only
+ *             columns j <= q are visible; out is exactly 0 for j > q.
+ * rowsum (nullable, fp32 [rows]) receives sum_j y_j + 1e-12 per row.
+ * x and out have the same dtype; ld_x / ld_out are row strides in elements.
+ * cols must be in [1, 4096]; power in {1,2,3}.
+ *
+ * Replaces: softplus_norm_triton_out / _softplus_norm_fwd
+ *             (src/smooth_attn/kernels.py:1006-1031, :494-531)
+ *           softplus_norm_causal_triton_out and its winner / tiered / generic
+ *             variants (src/smooth_attn/kernels.py:1274-1297, :565-676,
+ *             :1071-1172)
+ */
+SA_API int sa_norm_fwd(const void* x, void* out, float* rowsum, int64_t rows, int64_t cols, int64_t ld_x,
+                int64_t ld_out, int dtype, int causal, float alpha, float theta, int power, void* stream);
+
+/*
+ * Fused backward of sa_norm_fwd.
+ *   dx_j = (dy_j/dx_j / S) * (g_j - sum_k g_k y_k / S),  S = sum_k y_k + 1e-12
+ *   dy/dx = alpha * power * sp^(power-1) * sp',  sp' = (1 + a / sqrt(a^2+4)) / 2
+ * x and dx share `dtype`; g has `g_dtype` (any of SA_F32/SA_F16/SA_BF16).
+ * rowsum (nullable): the normalizer saved by sa_norm_fwd; when NULL it is
+ * recomputed.  dx is written for every column (exact 0 above the diagonal in
+ * causal mode).
+ *
+ * Replaces: _softplus_norm_causal_backward and the causal bwd kernels
+ *             (src/smooth_attn/kernels.py:1197-1230, :679-849)
+ */
+SA_API int sa_norm_bwd(const void* x, const void* g, const float* rowsum, void* dx, int64_t rows, int64_t cols,
+                int64_t ld_x, int64_t ld_g, int64_t ld_dx, int dtype, int g_dtype, int causal, float alpha,
+                float theta, int power, void* stream);
+
+/*
+ * Fused causal squareplus attention forward (tcgen05 / TMEM / TMA).
+ *   s = (q . k) * scale;  a = 2 s - 1;  y = ((a + sqrt(a^2+4)) / 2)^2 on the
+ *   causal (and optional sliding-window: q - k < window) prefix;
+ *   R = 1e-12 + sum y;  o = (sum bf16(y) v) / R.
+ * q, o: [B, Hq, T, D]; k, v: [B, Hkv, T, D]; Hq % Hkv == 0 (GQA).
+ * Strides are in elements as {batch, head, seq, dim}; the dim stride must be 1
+ * and the others multiples of 8 elements (16 B) with 16 B aligned bases.
+ * dtype: SA_BF16 or SA_F16.  D in {32, 64, 128}.
+ * rowsum: fp32 [B, Hq, T] contiguous, receives R (needed by the backward).
+ * exact_math = 0 computes sqrt(u) as u * rsqrt(u) (the reference's default).
+ *
+ * Replaces: _sp2norm_flash_fwd / _sp2norm_flash_fwd_with_rowsum_kernel
+ *             (src/smooth_attn/kernels.py:1912-1931, :1549-1631)
+ */
+SA_API int sa_flash_fwd(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B, int64_t Hq,
+                 int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                 const int64_t* v_strides, const int64_t* o_strides, float scale, int64_t window_size,
+                 int exact_math, int dtype, void* stream);
+
+/*
+ * Workspace size in bytes that sa_flash_bwd needs for the given problem
+ * (fp32 dQ accumulator + per-row delta).  The caller allocates it.
+ */
+SA_API int64_t sa_flash_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D);
+
+/*
+ * Fused causal squareplus attention backward.
+ *   delta = rowsum(dO * O); dP = dO V^T; dY = (dP - delta) / R;
+ *   dS = dY * 4 sp sp' * scale; dQ = dS K; dK = dS^T Q; dV = (y/R)^T dO
+ * (dK, dV summed over the query heads of a GQA group).
+ * q, o, dout, dq: [B, Hq, T, D]; k, v, dk, dv: [B, Hkv, T, D]; strides as in
+ * sa_flash_fwd (dq/dk/dv/dout may have their own strides).
+ * rowsum: fp32 [B, Hq, T] from sa_flash_fwd.  workspace: at least
+ * sa_flash_bwd_workspace_size() bytes, 256 B aligned, contents undefined on
+ * entry.
+ *
+ * Replaces: _sp2norm_flash_bwd, _sp2norm_flash_bwd_dq_kernel,
+ *           _sp2norm_flash_bwd_dkv_kernel
+ *             (src/smooth_attn/kernels.py:1934-1989, :1680-1784, :1800-1909)
+ */
+SA_API int sa_flash_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                 const float* rowsum, void* dq, void* dk, void* dv, void* workspace, int64_t workspace_bytes,
+                 int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides,
+                 const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                 const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                 const int64_t* dv_strides, float scale, int64_t window_size, int exact_math, int dtype,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMOOTH_ATTN_B200_H */

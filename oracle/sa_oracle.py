@@ -1,0 +1,237 @@
+"""CPU oracle for the smooth-attn hot path (TEST INFRASTRUCTURE ONLY).
+
+This module restates, in numpy, the reference's eager PyTorch algorithms for
+squareplus normalization and squareplus flash attention.  It is the checker
+the parity tests, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg compare the CUDA kernels against.  Nothing in the product package imports
+it; the product path has no CPU fallback.
+
+Parity pinning: every function here is checked against golden vectors that
+were produced by running the reference's own eager functions
+(``src/smooth_attn/kernels.py`` in NoSelection/smooth-attn) on seeded inputs;
+see ``tests/golden/gen_golden.py`` and ``tests/test_oracle_golden.py``.
+
+Reference citations (file:line inside NoSelection/smooth-attn):
+  * activation      ``src/smooth_attn/kernels.py:1328-1329``
+  * row-wise norm   ``src/smooth_attn/kernels.py:1332-1346``
+  * causal norm     ``src/smooth_attn/kernels.py:1349-1365``
+  * causal bwd      ``src/smooth_attn/kernels.py:679-743`` (the closed form the
+                    fused kernel uses; equals autograd of the eager causal norm)
+  * flash eager     ``src/smooth_attn/kernels.py:2053-2084``
+  * flash bwd       ``src/smooth_attn/kernels.py:1680-1909`` (closed form)
+  * EPS             ``src/smooth_attn/kernels.py:57``
+
+All arithmetic is float32 unless ``acc=np.float64`` is requested, matching the
+reference's fp32 eager path.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+EPS = 1e-12  # kernels.py:57
+SUPPORTED_POWERS = (1, 2, 3)  # kernels.py:24
+
+
+def _as_f(x, acc):
+    return np.asarray(x, dtype=acc)
+
+
+def squareplus(arg, acc=np.float32):
+    """sp(a) = 0.5 * (a + sqrt(a*a + 4))   (kernels.py:1328-1329)."""
+    arg = _as_f(arg, acc)
+    return acc(0.5) * (arg + np.sqrt(arg * arg + acc(4.0)))
+
+
+def family_activation(x, alpha, theta, power, acc=np.float32):
+    """y = sp(alpha*(x-theta))**power   (kernels.py:1340-1344)."""
+    if power not in SUPPORTED_POWERS:
+        raise ValueError(f"power must be one of {SUPPORTED_POWERS}, got {power}")
+    x = _as_f(x, acc)
+    y = squareplus(acc(alpha) * (x - acc(theta)), acc)
+    if power == 2:
+        y = y * y
+    elif power == 3:
+        y = y * y * y
+    return y
+
+
+def softplus_norm(x, alpha=2.0, theta=0.5, power=2, acc=np.float32):
+    """Row-wise normalization over the last axis (kernels.py:1332-1346)."""
+    y = family_activation(x, alpha, theta, power, acc)
+    return y / (y.sum(axis=-1, keepdims=True) + acc(EPS))
+
+
+def causal_mask(L):
+    """True where column j is visible to row q, i.e. j <= q (kernels.py:226-233 masks j > q)."""
+    return np.tril(np.ones((L, L), dtype=bool))
+
+
+def softplus_norm_causal(x, alpha=2.0, theta=0.5, power=2, acc=np.float32, return_rowsum=False):
+    """Causal normalization over the last two (square) axes (kernels.py:1349-1365).
+
+    Returns ``out`` (and the normalizer ``S = sum_vis y + EPS`` per row when
+    ``return_rowsum``), with exact zeros above the diagonal.
+    """
+    x = _as_f(x, acc)
+    L = x.shape[-1]
+    if x.shape[-2] != L:
+        raise ValueError("causal attention expects square score matrices on the last two dims")
+    y = family_activation(x, alpha, theta, power, acc)
+    y = np.where(causal_mask(L), y, acc(0.0))
+    s = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    out = y / s
+    if return_rowsum:
+        return out, s[..., 0]
+    return out
+
+
+def softplus_norm_causal_bwd(x, g, alpha=2.0, theta=0.5, power=2, acc=np.float32):
+    """Gradient of ``sum(softplus_norm_causal(x) * g)`` w.r.t. x.
+
+    Closed form used by the reference's fused backward (kernels.py:710-743):
+      a = alpha (x - theta); sp = 0.5 (a + sqrt(a^2+4)); sp' = 0.5 (1 + a/sqrt(a^2+4))
+      dy/dx = alpha * power * sp^(power-1) * sp'
+      p = y / S;  dX = (dy/dx / S) * (g - sum_k g_k p_k); zero above the diagonal.
+    """
+    x = _as_f(x, acc)
+    g = _as_f(g, acc)
+    L = x.shape[-1]
+    mask = causal_mask(L)
+    a = acc(alpha) * (x - acc(theta))
+    r = np.sqrt(a * a + acc(4.0))
+    sp = acc(0.5) * (a + r)
+    spp = acc(0.5) * (acc(1.0) + a / r)
+    if power == 1:
+        y = sp
+        dydx = acc(alpha) * spp
+    elif power == 2:
+        y = sp * sp
+        dydx = acc(alpha) * acc(2.0) * sp * spp
+    elif power == 3:
+        y = sp * sp * sp
+        dydx = acc(alpha) * acc(3.0) * sp * sp * spp
+    else:
+        raise ValueError(f"power must be one of {SUPPORTED_POWERS}, got {power}")
+    y = np.where(mask, y, acc(0.0))
+    g = np.where(mask, g, acc(0.0))
+    s = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    p = y / s
+    dot = (g * p).sum(axis=-1, keepdims=True)
+    dx = (dydx / s) * (g - dot)
+    return np.where(mask, dx, acc(0.0))
+
+
+def softplus_norm_bwd(x, g, alpha=2.0, theta=0.5, power=2, acc=np.float32):
+    """Row-wise (non-causal) analogue of :func:`softplus_norm_causal_bwd`."""
+    x = _as_f(x, acc)
+    g = _as_f(g, acc)
+    a = acc(alpha) * (x - acc(theta))
+    r = np.sqrt(a * a + acc(4.0))
+    sp = acc(0.5) * (a + r)
+    spp = acc(0.5) * (acc(1.0) + a / r)
+    y = sp ** power
+    dydx = acc(alpha) * acc(power) * sp ** (power - 1) * spp
+    s = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    dot = (g * (y / s)).sum(axis=-1, keepdims=True)
+    return (dydx / s) * (g - dot)
+
+
+def _expand_kv(k, n_q_heads):
+    """GQA: query head h reads kv head h // (H_q // H_kv)  (kernels.py:1568, 2058-2062)."""
+    h_kv = k.shape[1]
+    if h_kv == n_q_heads:
+        return k
+    return np.repeat(k, n_q_heads // h_kv, axis=1)
+
+
+def _flash_mask(T, window_size):
+    m = causal_mask(T)
+    if window_size > 0:
+        pos = np.arange(T)
+        m &= (pos[:, None] - pos[None, :]) < window_size  # kernels.py:2076-2079
+    return m
+
+
+def sp2norm_flash_attention(q, k, v, scale=None, window_size=0, acc=np.float32, return_rowsum=False):
+    """Eager squareplus attention (kernels.py:2053-2084).
+
+    q: [B, H_q, T, D]; k, v: [B, H_kv, T, D].  Returns o [B, H_q, T, D] in ``acc``
+    (and the normalizer R = sum_vis y + EPS, [B, H_q, T], when ``return_rowsum``).
+    """
+    q = _as_f(q, acc)
+    k = _expand_kv(_as_f(k, acc), q.shape[1])
+    v = _expand_kv(_as_f(v, acc), q.shape[1])
+    T, D = q.shape[-2], q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    s = np.matmul(q, np.swapaxes(k, -1, -2)) * acc(scale)
+    a = acc(2.0) * s - acc(1.0)
+    sp = acc(0.5) * (a + np.sqrt(a * a + acc(4.0)))
+    y = sp * sp
+    y = np.where(_flash_mask(T, window_size), y, acc(0.0))
+    r = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    o = np.matmul(y / r, v)
+    if return_rowsum:
+        return o, r[..., 0]
+    return o
+
+
+def sp2norm_flash_attention_bwd(q, k, v, do, scale=None, window_size=0, acc=np.float32):
+    """Gradients (dq, dk, dv) of ``sum(sp2norm_flash_attention(q,k,v) * do)``.
+
+    Closed form of the reference's fused backward (kernels.py:1723-1909):
+      delta = rowsum(dO * O); dP = dO V^T; dY = (dP - delta)/R;
+      dS = dY * 4 sp sp' * scale;  dQ = dS K;  dK = dS^T Q;  dV = (y/R)^T dO
+    GQA gradients of K/V are summed over the query heads of each group.
+    """
+    q = _as_f(q, acc)
+    k_in = _as_f(k, acc)
+    v_in = _as_f(v, acc)
+    do = _as_f(do, acc)
+    B, Hq, T, D = q.shape
+    Hkv = k_in.shape[1]
+    k = _expand_kv(k_in, Hq)
+    v = _expand_kv(v_in, Hq)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    s = np.matmul(q, np.swapaxes(k, -1, -2)) * acc(scale)
+    a = acc(2.0) * s - acc(1.0)
+    rt = np.sqrt(a * a + acc(4.0))
+    sp = acc(0.5) * (a + rt)
+    spp = acc(0.5) * (acc(1.0) + a / rt)
+    mask = _flash_mask(T, window_size)
+    y = np.where(mask, sp * sp, acc(0.0))
+    r = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    p = y / r
+    o = np.matmul(p, v)
+    delta = (do * o).sum(axis=-1, keepdims=True)
+    dp = np.matmul(do, np.swapaxes(v, -1, -2))
+    dy = np.where(mask, (dp - delta) / r, acc(0.0))
+    ds = dy * acc(4.0) * sp * spp * acc(scale)
+    dq = np.matmul(ds, k)
+    dk = np.matmul(np.swapaxes(ds, -1, -2), q)
+    dv = np.matmul(np.swapaxes(p, -1, -2), do)
+    if Hkv != Hq:
+        g = Hq // Hkv
+        dk = dk.reshape(B, Hkv, g, T, D).sum(axis=2)
+        dv = dv.reshape(B, Hkv, g, T, D).sum(axis=2)
+    return dq, dk, dv
+
+
+def flash_flops(B, H, T, D, window_size=0, bwd=False):
+    """Algorithmic FLOPs of causal squareplus attention.
+
+    Visible (q,k) pairs are counted exactly (causal triangle, optionally clipped
+    by the sliding window); forward = 2 GEMMs (QK^T, PV), backward = 5 GEMMs
+    (QK^T recompute, dO V^T, dV, dK, dQ), each 2*D flops per visible pair.
+    """
+    if window_size and window_size < T:
+        w = window_size
+        vis = w * (w + 1) // 2 + (T - w) * w
+    else:
+        vis = T * (T + 1) // 2
+    gemms = 5 if bwd else 2
+    return 2 * D * vis * B * H * gemms

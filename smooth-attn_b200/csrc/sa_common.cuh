@@ -1,0 +1,68 @@
+// Shared device helpers for the smooth-attn B200 kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/smooth_attn_b200.h"
+
+#define SA_EPS 1e-12f  // src/smooth_attn/kernels.py:57
+
+namespace sa {
+
+// ---- element conversion ----------------------------------------------------
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// A 16-byte register bundle viewed as VEC elements of T (VEC = 16 / sizeof(T)),
+// or a single element when VEC == 1.
+template <typename T, int VEC> struct Pack;
+template <typename T> struct Pack<T, 1> {
+  T v;
+  __device__ __forceinline__ float get(int) const { return to_f<T>(v); }
+  __device__ __forceinline__ void set(int, float f) { v = from_f<T>(f); }
+  __device__ __forceinline__ void zero() { v = from_f<T>(0.f); }
+};
+template <typename T, int VEC> struct Pack {
+  static_assert(VEC * sizeof(T) == 16, "vector pack must be 16 bytes");
+  union {
+    uint4 u;
+    T e[VEC];
+  };
+  __device__ __forceinline__ float get(int i) const { return to_f<T>(e[i]); }
+  __device__ __forceinline__ void set(int i, float f) { e[i] = from_f<T>(f); }
+  __device__ __forceinline__ void zero() { u = make_uint4(0, 0, 0, 0); }
+};
+
+// Streaming (read-once) load and streaming store.
+template <typename T, int VEC>
+__device__ __forceinline__ void load_stream(Pack<T, VEC>& p, const T* ptr) {
+  if constexpr (VEC == 1) {
+    p.v = __ldcs(ptr);
+  } else {
+    p.u = __ldcs(reinterpret_cast<const uint4*>(ptr));
+  }
+}
+template <typename T, int VEC>
+__device__ __forceinline__ void store_stream(T* ptr, const Pack<T, VEC>& p) {
+  if constexpr (VEC == 1) {
+    __stcs(ptr, p.v);
+  } else {
+    __stcs(reinterpret_cast<uint4*>(ptr), p.u);
+  }
+}
+
+// sqrt(u) as u * rsqrt(u): one MUFU op, the reference's `_fast_sqrt`
+// (src/smooth_attn/kernels.py:467-470).  u >= 4 here, so no 0/inf cases.
+__device__ __forceinline__ float fast_sqrt(float u) { return u * rsqrtf(u); }
+
+}  // namespace sa

@@ -1,0 +1,92 @@
+"""ctypes binding of the C ABI in ``include/smooth_attn_b200.h``.
+
+The shared library ``libsmooth_attn_b200.so`` sits next to this file (built
+in-tree by ``smooth-attn_b200/build.py``).  There is no fallback: if the
+library is missing or cannot be loaded, every kernel entry point raises
+``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).with_name("libsmooth_attn_b200.so")
+
+SA_OK = 0
+SA_ERR_ARG = -1
+SA_ERR_ALIGN = -2
+SA_ERR_UNSUPPORTED = -3
+SA_ERR_LAUNCH = -4
+SA_ERR_TIMEOUT = -5
+SA_ERR_CUDA = -6
+
+SA_F32, SA_F16, SA_BF16 = 0, 1, 2
+
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_f = ctypes.c_float
+_p = ctypes.c_void_p
+_i64p = ctypes.POINTER(ctypes.c_int64)
+
+# name -> (restype, argtypes); mirrors include/smooth_attn_b200.h
+SIGNATURES = {
+    "sa_version": (_int, []),
+    "sa_status_string": (ctypes.c_char_p, [_int]),
+    "sa_last_cuda_error": (ctypes.c_char_p, []),
+    "sa_norm_fwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _int, _int, _f, _f, _int, _p]),
+    "sa_norm_bwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _f, _f, _int, _p]),
+    "sa_flash_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                            _i64p, _i64p, _i64p, _i64p, _f, _i64, _int, _int, _p]),
+    "sa_flash_bwd_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "sa_flash_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+                            _i64, _i64, _i64, _i64, _i64,
+                            _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
+                            _f, _i64, _int, _int, _p]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: Path | str | None = None):
+    """Load (once) and return the ctypes library handle; raise if unavailable."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"{p.name} is not built (expected at {p}); run `python smooth-attn_b200/build.py`. "
+                "smooth_attn has no CPU or Triton fallback."
+            )
+        lib = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+def check(status: int, what: str):
+    """Map a C-ABI status to the reference's exception types."""
+    if status == SA_OK:
+        return
+    lib = load()
+    msg = lib.sa_status_string(status).decode()
+    if status in (SA_ERR_ARG, SA_ERR_UNSUPPORTED, SA_ERR_ALIGN):
+        raise ValueError(f"{what}: {msg}")
+    detail = lib.sa_last_cuda_error().decode()
+    raise KernelError(f"{what}: {msg} {detail}".strip())
+
+
+def strides(t):
+    return (ctypes.c_int64 * 4)(*t.stride())

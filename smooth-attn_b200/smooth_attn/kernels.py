@@ -1,0 +1,569 @@
+"""Public API of smooth-attn, backed by hand-written sm_100a CUDA kernels.
+
+Same names, signatures, argument meaning and exception types as the
+reference package (NoSelection/smooth-attn ``src/smooth_attn/kernels.py``);
+the ``*_triton*`` names are kept for drop-in compatibility although no Triton
+is involved.  Every hot-path call validates on the host, then calls the C ABI
+of ``libsmooth_attn_b200.so`` (``include/smooth_attn_b200.h``) on torch's
+current CUDA stream.  There is no CPU or Triton fallback: on a machine
+without the built library the kernel entry points raise ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+SUPPORTED_POWERS = (1, 2, 3)  # kernels.py:24
+SUPPORTED_DTYPES = {  # kernels.py:25-29
+    "fp32": torch.float32,
+    "fp16": torch.float16,
+    "bf16": torch.bfloat16,
+}
+EPS = 1e-12  # kernels.py:57
+MAX_ROW_COLS = 4096  # kernels.py:236-240 (largest row the fused row kernels accept)
+FLASH_HEAD_DIMS = (32, 64, 128)
+
+_DTYPE_CODE = {torch.float32: _lib.SA_F32, torch.float16: _lib.SA_F16, torch.bfloat16: _lib.SA_BF16}
+_CAUSAL_MASK_CACHE: dict = {}
+
+
+@dataclass(frozen=True)
+class FamilyConfig:
+    """squareplus(alpha * (x - theta))^power / sum  (kernels.py:65-89)."""
+
+    alpha: float = 2.0
+    theta: float = 0.5
+    power: int = 2
+
+    def __post_init__(self):
+        if self.power not in SUPPORTED_POWERS:
+            raise ValueError(f"power must be one of {SUPPORTED_POWERS}, got {self.power}")
+
+    @property
+    def cache_key(self):
+        return (float(self.alpha), float(self.theta), int(self.power))
+
+    @property
+    def kernel_kwargs(self):
+        return {"ALPHA": float(self.alpha), "THETA": float(self.theta), "POWER": int(self.power)}
+
+    @property
+    def label(self):
+        return f"squareplus({self.alpha:g} * (x - {self.theta:g}))^{self.power} / sum"
+
+
+@dataclass(frozen=True)
+class RowwiseBenchmarkResult:
+    shape: tuple
+    torch_softmax_us: float
+    triton_softmax_us: float
+    family_us: float
+
+
+@dataclass(frozen=True)
+class CausalBenchmarkResult:
+    dtype: torch.dtype
+    batch: int
+    heads: int
+    seq_len: int
+    torch_softmax_us: float
+    triton_softmax_us: float
+    family_us: float
+    softmax_err: float
+    family_err: float
+    softmax_sums_ok: bool
+    family_sums_ok: bool
+    softmax_meta: dict
+    family_meta: dict
+
+
+DEFAULT_FAMILY = FamilyConfig()
+BENCH_ALPHA = DEFAULT_FAMILY.alpha
+BENCH_THETA = DEFAULT_FAMILY.theta
+BENCH_POWER = DEFAULT_FAMILY.power
+
+
+# ---------------------------------------------------------------------------
+# validation (error conventions of kernels.py:167-223)
+# ---------------------------------------------------------------------------
+
+
+def _resolve_family(alpha, theta, power, family):
+    if family is None:
+        return FamilyConfig(alpha=alpha, theta=theta, power=power)
+    if (alpha, theta, power) != (DEFAULT_FAMILY.alpha, DEFAULT_FAMILY.theta, DEFAULT_FAMILY.power):
+        raise ValueError("pass either family=... or alpha/theta/power overrides, not both")
+    return family
+
+
+def _validate_cuda_tensor(x, *, name):
+    if not isinstance(x, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not x.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if x.dtype not in SUPPORTED_DTYPES.values():
+        raise ValueError(f"{name} dtype must be one of {tuple(SUPPORTED_DTYPES.values())}, got {x.dtype}")
+
+
+def _check_cols(n_cols):
+    if n_cols > MAX_ROW_COLS:
+        raise ValueError(f"n_cols={n_cols} is too large for this fused row kernel")
+
+
+def _prepare_rowwise_input(x):
+    _validate_cuda_tensor(x, name="x")
+    if x.ndim != 2:
+        raise ValueError(f"row-wise kernels expect a 2D tensor, got shape {tuple(x.shape)}")
+    return x if x.is_contiguous() else x.contiguous()
+
+
+def _prepare_attention_input(x):
+    _validate_cuda_tensor(x, name="x")
+    if x.ndim < 2:
+        raise ValueError("attention scores must have at least 2 dimensions")
+    if x.shape[-1] != x.shape[-2]:
+        raise ValueError("causal attention expects square score matrices on the last two dims")
+    return x if x.is_contiguous() else x.contiguous()
+
+
+def _prepare_output(out, reference):
+    _validate_cuda_tensor(out, name="out")
+    if out.shape != reference.shape:
+        raise ValueError(f"out shape {tuple(out.shape)} must match input shape {tuple(reference.shape)}")
+    if out.dtype != reference.dtype:
+        raise ValueError(f"out dtype {out.dtype} must match input dtype {reference.dtype}")
+    if out.device != reference.device:
+        raise ValueError("out and input must live on the same CUDA device")
+    if out.is_contiguous():
+        return out, None
+    return torch.empty_like(reference), out
+
+
+def _finalize_output(kernel_out, user_out):
+    if user_out is None:
+        return kernel_out
+    user_out.copy_(kernel_out)
+    return user_out
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _is_winner_family(family):
+    return family.cache_key == DEFAULT_FAMILY.cache_key
+
+
+# ---------------------------------------------------------------------------
+# normalization forward / backward launchers
+# ---------------------------------------------------------------------------
+
+
+def _launch_norm_fwd(x2d, out2d, family, causal, rowsum=None):
+    """x2d/out2d: contiguous [rows, cols] CUDA tensors of the same dtype."""
+    rows, cols = x2d.shape
+    _check_cols(cols)
+    with torch.cuda.device(x2d.device):
+        st = _lib.load().sa_norm_fwd(
+            x2d.data_ptr(), out2d.data_ptr(), rowsum.data_ptr() if rowsum is not None else None,
+            rows, cols, max(x2d.stride(0), cols), max(out2d.stride(0), cols),
+            _DTYPE_CODE[x2d.dtype], int(causal), float(family.alpha), float(family.theta), int(family.power),
+            _stream(x2d),
+        )
+    _lib.check(st, "sa_norm_fwd")
+    variant = ("squareplus_winner" if _is_winner_family(family) else "squareplus_family") + "_b200"
+    return {"variant": variant, "causal": bool(causal), "rows": rows, "cols": cols, "kernel": "sa_norm_fwd"}
+
+
+def _launch_norm_bwd(x2d, g2d, rowsum, dx2d, family, causal):
+    rows, cols = x2d.shape
+    _check_cols(cols)
+    with torch.cuda.device(x2d.device):
+        st = _lib.load().sa_norm_bwd(
+            x2d.data_ptr(), g2d.data_ptr(), rowsum.data_ptr() if rowsum is not None else None, dx2d.data_ptr(),
+            rows, cols, max(x2d.stride(0), cols), max(g2d.stride(0), cols), max(dx2d.stride(0), cols),
+            _DTYPE_CODE[x2d.dtype], _DTYPE_CODE[g2d.dtype], int(causal),
+            float(family.alpha), float(family.theta), int(family.power), _stream(x2d),
+        )
+    _lib.check(st, "sa_norm_bwd")
+
+
+# ---------------------------------------------------------------------------
+# row-wise normalization (kernels.py:985-1035)
+# ---------------------------------------------------------------------------
+
+
+def softplus_norm_triton(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta, power=DEFAULT_FAMILY.power,
+                         *, family=None, return_meta=False):
+    family = _resolve_family(alpha, theta, power, family)
+    x_row = _prepare_rowwise_input(x)
+    _check_cols(x_row.shape[1])
+    out = torch.empty_like(x_row)
+    meta = _launch_norm_fwd(x_row, out, family, causal=False)
+    return (out, meta) if return_meta else out
+
+
+def softplus_norm_triton_out(out, x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta,
+                             power=DEFAULT_FAMILY.power, *, family=None, return_meta=False):
+    family = _resolve_family(alpha, theta, power, family)
+    x_row = _prepare_rowwise_input(x)
+    kernel_out, user_out = _prepare_output(out, x_row)
+    _check_cols(x_row.shape[1])
+    meta = _launch_norm_fwd(x_row, kernel_out, family, causal=False)
+    result = _finalize_output(kernel_out, user_out)
+    return (result, meta) if return_meta else result
+
+
+def sp2norm_triton(x, return_meta=False):
+    return softplus_norm_triton(x, family=DEFAULT_FAMILY, return_meta=return_meta)
+
+
+# ---------------------------------------------------------------------------
+# causal normalization (kernels.py:1254-1297)
+# ---------------------------------------------------------------------------
+
+
+def _causal_out(out, x_attn, family, rowsum=None):
+    kernel_out, user_out = _prepare_output(out, x_attn)
+    L = x_attn.shape[-1]
+    _check_cols(L)
+    meta = _launch_norm_fwd(x_attn.view(-1, L), kernel_out.view(-1, L), family, causal=True, rowsum=rowsum)
+    return _finalize_output(kernel_out, user_out), meta
+
+
+def softplus_norm_causal_triton(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta,
+                                power=DEFAULT_FAMILY.power, *, family=None, return_meta=False):
+    family = _resolve_family(alpha, theta, power, family)
+    x_attn = _prepare_attention_input(x)
+    out = torch.empty_like(x_attn)
+    return softplus_norm_causal_triton_out(out, x_attn, family=family, return_meta=return_meta)
+
+
+def softplus_norm_causal_triton_out(out, x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta,
+                                    power=DEFAULT_FAMILY.power, *, family=None, return_meta=False):
+    family = _resolve_family(alpha, theta, power, family)
+    x_attn = _prepare_attention_input(x)
+    result, meta = _causal_out(out, x_attn, family)
+    return (result, meta) if return_meta else result
+
+
+class _SoftplusNormCausalAutogradFn(torch.autograd.Function):
+    """kernels.py:1373-1398, but saving the fp32 row normalizer with x and
+    running the fused CUDA backward directly on dY's own dtype (no fp32 copy)."""
+
+    @staticmethod
+    def forward(ctx, x, alpha, theta, power):
+        family = FamilyConfig(alpha=float(alpha), theta=float(theta), power=int(power))
+        x_attn = _prepare_attention_input(x)
+        L = x_attn.shape[-1]
+        out = torch.empty_like(x_attn)
+        rowsum = torch.empty(x_attn.numel() // max(L, 1), device=x_attn.device, dtype=torch.float32)
+        result, _ = _causal_out(out, x_attn, family, rowsum=rowsum)
+        ctx.family = family
+        ctx.save_for_backward(x_attn, rowsum)
+        return result
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        if not ctx.needs_input_grad[0]:
+            return None, None, None, None
+        x, rowsum = ctx.saved_tensors
+        L = x.shape[-1]
+        g = grad_output.contiguous()
+        dx = torch.empty_like(x)
+        _launch_norm_bwd(x.view(-1, L), g.view(-1, L), rowsum, dx.view(-1, L), ctx.family, causal=True)
+        return dx, None, None, None
+
+
+def softplus_norm_causal(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta, power=DEFAULT_FAMILY.power,
+                         *, family=None, implementation="triton"):
+    family = _resolve_family(alpha, theta, power, family)
+    if implementation == "triton":
+        return _SoftplusNormCausalAutogradFn.apply(x, family.alpha, family.theta, family.power)
+    if implementation == "eager":
+        return softplus_norm_causal_eager(x.float(), family=family).to(x.dtype)
+    raise ValueError("implementation must be 'triton' or 'eager'")
+
+
+class SoftplusNormCausal(torch.nn.Module):
+    def __init__(self, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta, power=DEFAULT_FAMILY.power, *,
+                 family=None, implementation="triton"):
+        super().__init__()
+        self.family = _resolve_family(alpha, theta, power, family)
+        self.implementation = implementation
+
+    def forward(self, x):
+        return softplus_norm_causal(x, family=self.family, implementation=self.implementation)
+
+
+# ---------------------------------------------------------------------------
+# eager torch functions (public API of the reference, kernels.py:1328-1370,
+# 2053-2084).  They are plain torch code on whatever device x lives on; they
+# are the user-facing "eager" implementation, not a fallback of the kernels.
+# ---------------------------------------------------------------------------
+
+
+def _causal_mask(seq_len, device):
+    key = (device.type, device.index, seq_len)
+    if key not in _CAUSAL_MASK_CACHE:
+        _CAUSAL_MASK_CACHE[key] = torch.triu(torch.ones(seq_len, seq_len, device=device, dtype=torch.bool), 1)
+    return _CAUSAL_MASK_CACHE[key]
+
+
+def _apply_family_activation_eager(arg):
+    return 0.5 * (arg + torch.sqrt(arg * arg + 4.0))
+
+
+def _family_y_eager(x, family):
+    y = _apply_family_activation_eager(family.alpha * (x - family.theta))
+    if family.power == 2:
+        y = y * y
+    elif family.power == 3:
+        y = y * y * y
+    return y
+
+
+def softplus_norm_eager(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta, power=DEFAULT_FAMILY.power, *,
+                        family=None):
+    family = _resolve_family(alpha, theta, power, family)
+    y = _family_y_eager(x, family)
+    return y / (y.sum(dim=-1, keepdim=True) + EPS)
+
+
+def softplus_norm_causal_eager(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta,
+                               power=DEFAULT_FAMILY.power, *, family=None):
+    family = _resolve_family(alpha, theta, power, family)
+    y = _family_y_eager(x, family).masked_fill(_causal_mask(x.shape[-1], x.device), 0.0)
+    return y / (y.sum(dim=-1, keepdim=True) + EPS)
+
+
+def softmax_causal_eager(x):
+    return F.softmax(x.masked_fill(_causal_mask(x.shape[-1], x.device), float("-inf")), dim=-1)
+
+
+def sp2norm_flash_attention_eager(q, k, v, *, scale=None, window_size=0):
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if H_kv < H_q:
+        g = H_q // H_kv
+        k = k.unsqueeze(2).expand(B, H_kv, g, T, D).reshape(B, H_q, T, D)
+        v = v.unsqueeze(2).expand(B, H_kv, g, T, D).reshape(B, H_q, T, D)
+    s = torch.matmul(q.float(), k.float().transpose(-2, -1)) * scale
+    arg = 2.0 * s - 1.0
+    sp = 0.5 * (arg + torch.sqrt(arg * arg + 4.0))
+    y = (sp * sp).masked_fill(_causal_mask(T, q.device), 0.0)
+    if window_size > 0:
+        pos = torch.arange(T, device=q.device)
+        y = y.masked_fill(((pos[:, None] - pos[None, :]) >= window_size)[None, None], 0.0)
+    attn = y / (y.sum(dim=-1, keepdim=True) + EPS)
+    return torch.matmul(attn, v.float()).to(q.dtype)
+
+
+# ---------------------------------------------------------------------------
+# softmax baselines: comparison only, outside the hot path; backed by torch
+# with the reference's validation (kernels.py:1233-1251, 1300-1325).
+# ---------------------------------------------------------------------------
+
+
+def softmax_triton(x, return_meta=False):
+    x_row = _prepare_rowwise_input(x)
+    out = torch.softmax(x_row, dim=-1)
+    return (out, {"variant": "torch_softmax"}) if return_meta else out
+
+
+def softmax_triton_out(out, x, return_meta=False):
+    x_row = _prepare_rowwise_input(x)
+    kernel_out, user_out = _prepare_output(out, x_row)
+    torch.softmax(x_row, dim=-1, out=kernel_out)
+    result = _finalize_output(kernel_out, user_out)
+    return (result, {"variant": "torch_softmax"}) if return_meta else result
+
+
+def softmax_causal_triton(x, return_meta=False):
+    x_attn = _prepare_attention_input(x)
+    out = softmax_causal_eager(x_attn.float()).to(x_attn.dtype)
+    return (out, {"variant": "torch_softmax_causal"}) if return_meta else out
+
+
+def softmax_causal_triton_out(out, x, return_meta=False):
+    x_attn = _prepare_attention_input(x)
+    kernel_out, user_out = _prepare_output(out, x_attn)
+    kernel_out.copy_(softmax_causal_eager(x_attn.float()))
+    result = _finalize_output(kernel_out, user_out)
+    return (result, {"variant": "torch_softmax_causal"}) if return_meta else result
+
+
+# ---------------------------------------------------------------------------
+# fused squareplus flash attention (kernels.py:1912-2050)
+# ---------------------------------------------------------------------------
+
+
+def _flash_ready(t):
+    """TMA needs unit dim stride and 16-byte aligned base/strides; copy otherwise."""
+    es = t.element_size()
+    ok = (t.stride(3) == 1 and t.data_ptr() % 16 == 0
+          and all((s * es) % 16 == 0 for s in t.stride()[:3]))
+    return t if ok else t.contiguous()
+
+
+def _flash_check(q, k, v):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _validate_cuda_tensor(t, name=name)
+    if q.dtype not in (torch.bfloat16, torch.float16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError(f"flash attention needs bf16 or fp16 q/k/v of one dtype, got {q.dtype}/{k.dtype}/{v.dtype}")
+    if q.shape[-1] not in FLASH_HEAD_DIMS:
+        raise ValueError(f"head dim {q.shape[-1]} not supported (supported: {FLASH_HEAD_DIMS})")
+
+
+def _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True):
+    """Run the fused forward; return (o, row_sums) like kernels.py:1912-1931."""
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    o = torch.empty_like(q)
+    if not (o.stride(3) == 1 and all((s * o.element_size()) % 16 == 0 for s in o.stride()[:3])):
+        o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    row_sums = torch.empty(B, H_q, T, device=q.device, dtype=torch.float32)
+    if q.numel() == 0:
+        return o, row_sums
+    with torch.cuda.device(q.device):
+        st = _lib.load().sa_flash_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
+            B, H_q, H_kv, T, D, _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o),
+            float(scale), int(window_size), int(not use_fast_sqrt), _DTYPE_CODE[q.dtype], _stream(q),
+        )
+    _lib.check(st, "sa_flash_fwd")
+    return o, row_sums
+
+
+def _sp2norm_flash_bwd(q, k, v, o, do, row_sums, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True):
+    """Run the fused backward; return (dq, dk, dv) like kernels.py:1934-1989."""
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    do = _flash_ready(do)
+    dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    dk = torch.empty(k.shape, device=q.device, dtype=q.dtype)
+    dv = torch.empty(v.shape, device=q.device, dtype=q.dtype)
+    if q.numel() == 0:
+        return dq, dk.zero_(), dv.zero_()
+    lib = _lib.load()
+    ws_bytes = int(lib.sa_flash_bwd_workspace_size(B, H_q, H_kv, T, D))
+    ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
+    with torch.cuda.device(q.device):
+        st = lib.sa_flash_bwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), row_sums.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
+            B, H_q, H_kv, T, D,
+            _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o), _lib.strides(do),
+            _lib.strides(dq), _lib.strides(dk), _lib.strides(dv),
+            float(scale), int(window_size), int(not use_fast_sqrt), _DTYPE_CODE[q.dtype], _stream(q),
+        )
+    _lib.check(st, "sa_flash_bwd")
+    return dq, dk, dv
+
+
+class _SP2NormFlashAttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt):
+        q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
+        o, row_sums = _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt)
+        ctx.save_for_backward(q, k, v, o, row_sums)
+        ctx.scale = scale
+        ctx.n_kv_groups = n_kv_groups
+        ctx.window_size = window_size
+        ctx.use_fast_sqrt = use_fast_sqrt
+        return o
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, o, row_sums = ctx.saved_tensors
+        dq, dk, dv = _sp2norm_flash_bwd(q, k, v, o, grad_output, row_sums, ctx.scale, ctx.n_kv_groups,
+                                        ctx.window_size, use_fast_sqrt=ctx.use_fast_sqrt)
+        return dq, dk, dv, None, None, None, None
+
+
+def sp2norm_flash_attention(q, k, v, *, scale=None, window_size=0, exact_math=False):
+    """Fused QK^T -> squareplus norm -> V without materializing the T x T scores.
+
+    Supports autograd, GQA/MQA and sliding windows (kernels.py:2016-2050).
+    q: [B, H_q, T, D]; k, v: [B, H_kv, T, D] (any strides); bf16 or fp16;
+    D in {32, 64, 128}.
+    """
+    assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    assert k.shape == (B, H_kv, T, D) and v.shape == (B, H_kv, T, D)
+    assert H_q % H_kv == 0, f"H_q ({H_q}) must be divisible by H_kv ({H_kv})"
+    _flash_check(q, k, v)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    return _SP2NormFlashAttentionFn.apply(q, k, v, scale, H_q // H_kv, window_size, not exact_math)
+
+
+# ---------------------------------------------------------------------------
+# forward-only extensions outside this build's hot path (kernels.py:2093-2829)
+# ---------------------------------------------------------------------------
+
+
+def precompute_rope_cos_sin(dim, seq_len, base=10000.0, device="cuda", dtype=torch.float32):
+    """cos/sin tables for RoPE, each [T, D/2] (kernels.py:2093-2101)."""
+    inv_freq = 1.0 / (base ** (torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim))
+    t = torch.arange(seq_len, device=device, dtype=torch.float32)
+    freqs = torch.outer(t, inv_freq)
+    return freqs.cos().to(dtype), freqs.sin().to(dtype)
+
+
+def _not_built(name, ref):
+    def fn(*args, **kwargs):
+        raise NotImplementedError(
+            f"{name} ({ref}) is not part of this build's B200 hot path yet; "
+            "use sp2norm_flash_attention for fused squareplus attention"
+        )
+
+    fn.__name__ = name
+    return fn
+
+
+sp2norm_rope_flash_attention = _not_built("sp2norm_rope_flash_attention", "kernels.py:2373-2430")
+sp2norm_rope_flash_attention_proj = _not_built("sp2norm_rope_flash_attention_proj", "kernels.py:2433-2490")
+sp2norm_fp8_flash_attention = _not_built("sp2norm_fp8_flash_attention", "kernels.py:2630-2673")
+sp2norm_paged_attention = _not_built("sp2norm_paged_attention", "kernels.py:2776-2829")
+
+
+# ---------------------------------------------------------------------------
+# timing helpers (kernels.py:2832-2838)
+# ---------------------------------------------------------------------------
+
+
+def _median_cuda_us(fn, warmup=50, iters=200):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1000.0)
+    times.sort()
+    return times[len(times) // 2]
+
+
+def bench(fn, x=None, warmup=300, iters=1000):
+    callback = (lambda: fn(x)) if x is not None else fn
+    return _median_cuda_us(callback, warmup=warmup, iters=iters)
+
+
+def bench_out(fn, out, x, warmup=300, iters=1000):
+    return _median_cuda_us(lambda: fn(out, x), warmup=warmup, iters=iters)

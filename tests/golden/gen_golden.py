@@ -1,0 +1,114 @@
+"""Generate golden vectors from the reference's OWN eager implementation.
+
+Run in a container that has the reference checkout (read-only) at
+``$SMOOTH_ATTN_REF`` (default ``/root/reference``):
+
+    python tests/golden/gen_golden.py
+
+It imports ``smooth_attn`` from ``$SMOOTH_ATTN_REF/src`` and evaluates, on CPU
+in float32 with seeded ``torch.Generator`` inputs:
+  * ``softplus_norm_eager``               (kernels.py:1332-1346)
+  * ``softplus_norm_causal_eager``        (kernels.py:1349-1365) + torch autograd
+  * ``sp2norm_flash_attention_eager``     (kernels.py:2053-2084) + torch autograd
+
+and writes ``golden.npz`` next to this script.  The GPU box never runs this
+script (the reference is not present there); the tests only read the
+committed ``golden.npz``.  Inputs of bf16 cases are stored after rounding to
+bf16 (as float32), so a consumer can rebuild the exact bf16 tensors.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REF = Path(os.environ.get("SMOOTH_ATTN_REF", "/root/reference"))
+sys.path.insert(0, str(REF / "src"))
+
+import smooth_attn as ref  # noqa: E402  (the reference package)
+
+OUT = Path(__file__).with_name("golden.npz")
+
+
+def randn(shape, seed, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    t = torch.randn(*shape, generator=g, dtype=torch.float32)
+    return t.to(dtype).float()
+
+
+def main():
+    data = {}
+
+    # --- causal norm, forward + autograd backward --------------------------
+    causal_cases = [
+        # name, shape, (alpha, theta, power), input dtype
+        ("c_cfg1", (1, 2, 128, 128), (2.0, 0.5, 2), torch.float32),
+        ("c_p3", (1, 2, 64, 64), (1.5, 0.25, 3), torch.float32),
+        ("c_p1", (1, 1, 48, 48), (1.0, 0.0, 1), torch.float32),
+        ("c_l1", (1, 1, 1, 1), (2.0, 0.5, 2), torch.float32),
+        ("c_l7", (2, 1, 7, 7), (2.0, 0.5, 2), torch.float32),
+        ("c_l17", (1, 3, 17, 17), (2.0, 0.5, 2), torch.float32),
+        ("c_l129", (1, 1, 129, 129), (2.0, 0.5, 2), torch.float32),
+        ("c_bf16", (1, 2, 64, 64), (2.0, 0.5, 2), torch.bfloat16),
+        ("c_3d", (3, 40, 40), (2.0, 0.5, 2), torch.float32),
+    ]
+    for i, (name, shape, (a, t, p), dt) in enumerate(causal_cases):
+        fam = ref.FamilyConfig(alpha=a, theta=t, power=p)
+        x = randn(shape, 1000 + i, dt).requires_grad_(True)
+        g = randn(shape, 2000 + i)
+        y = ref.softplus_norm_causal_eager(x, family=fam)
+        (y * g).sum().backward()
+        data[f"{name}/x"] = x.detach().numpy()
+        data[f"{name}/g"] = g.numpy()
+        data[f"{name}/out"] = y.detach().numpy()
+        data[f"{name}/dx"] = x.grad.numpy()
+        data[f"{name}/family"] = np.array([a, t, p], dtype=np.float64)
+
+    # --- row-wise norm forward ---------------------------------------------
+    row_cases = [
+        ("r_64x96", (64, 96), (2.0, 0.5, 2)),
+        ("r_p3", (16, 250), (1.5, 0.25, 3)),
+        ("r_odd", (5, 33), (0.7, -0.3, 1)),
+    ]
+    for i, (name, shape, (a, t, p)) in enumerate(row_cases):
+        x = randn(shape, 3000 + i)
+        y = ref.softplus_norm_eager(x, alpha=a, theta=t, power=p)
+        data[f"{name}/x"] = x.numpy()
+        data[f"{name}/out"] = y.numpy()
+        data[f"{name}/family"] = np.array([a, t, p], dtype=np.float64)
+
+    # --- flash attention, forward + autograd backward ----------------------
+    flash_cases = [
+        # name, B, Hq, Hkv, T, D, window
+        ("f_mha", 1, 2, 2, 64, 32, 0),
+        ("f_gqa_win", 1, 4, 2, 48, 32, 16),
+        ("f_d64", 1, 1, 1, 80, 64, 0),
+        ("f_d128", 1, 1, 1, 40, 128, 0),
+    ]
+    for i, (name, B, Hq, Hkv, T, D, W) in enumerate(flash_cases):
+        q = randn((B, Hq, T, D), 4000 + i, torch.bfloat16).requires_grad_(True)
+        k = randn((B, Hkv, T, D), 5000 + i, torch.bfloat16).requires_grad_(True)
+        v = randn((B, Hkv, T, D), 6000 + i, torch.bfloat16).requires_grad_(True)
+        do = randn((B, Hq, T, D), 7000 + i)
+        o = ref.sp2norm_flash_attention_eager(q, k, v, window_size=W)
+        (o * do).sum().backward()
+        data[f"{name}/q"] = q.detach().numpy()
+        data[f"{name}/k"] = k.detach().numpy()
+        data[f"{name}/v"] = v.detach().numpy()
+        data[f"{name}/do"] = do.numpy()
+        data[f"{name}/o"] = o.detach().numpy()
+        data[f"{name}/dq"] = q.grad.numpy()
+        data[f"{name}/dk"] = k.grad.numpy()
+        data[f"{name}/dv"] = v.grad.numpy()
+        data[f"{name}/window"] = np.array(W)
+
+    np.savez_compressed(OUT, **data)
+    print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(data)} arrays)")
+
+
+if __name__ == "__main__":
+    main()
