@@ -69,24 +69,27 @@ class ClockSampler:
         self.lines = []
 
     def __enter__(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+        q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            time.sleep(0.5)  # let nvidia-smi start before the timed region
         except (FileNotFoundError, OSError):
             self.proc = None
+        self.t_start = time.time()
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
     def __exit__(self, *exc):
+        self.t_end = time.time()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -97,9 +100,9 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 7:
+        for t, ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")][1:]  # drop nvidia-smi's timestamp
+            if len(parts) < 7 or not (self.t_start <= t <= self.t_end + 0.06):
                 continue
             try:
                 sm.append(float(parts[0]))
@@ -264,7 +267,7 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
 
     for _ in range(max(args.warmup, 3)):
         step()
-    steps = max(1, args.steps)
+    steps = max(3, args.steps // 200)
     ms = time_steps(step, steps, world) / steps
     flops_all = world * (O.flash_flops(B, H, T, D) + O.flash_flops(B, H, T, D, bwd=True))
     flops_loc = O.flash_flops(1, b_loc, T, D) + O.flash_flops(1, b_loc, T, D, bwd=True)
@@ -342,7 +345,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--skip-flash", action="store_true")

@@ -51,6 +51,15 @@ SA_API const char* sa_status_string(int status);
 SA_API const char* sa_last_cuda_error(void);
 
 /*
+ * Device-side status of the current device: SA_ERR_TIMEOUT if any kernel of
+ * this library gave up a bounded wait (an mbarrier / copy that never
+ * completed) since the last reset, else SA_OK.  Synchronises the device.
+ * reset != 0 clears the recorded status.  (No reference counterpart: the
+ * reference's Triton kernels have no bounded waits.)
+ */
+SA_API int sa_device_status(int reset);
+
+/*
  * Squareplus normalization forward over rows of length `cols`.
  *   y_j = squareplus(alpha * (x_j - theta))^power,  squareplus(a) = (a + sqrt(a^2+4)) / 2
  *   out_j = y_j / (sum_j y_j + 1e-12)

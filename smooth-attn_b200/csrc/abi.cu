@@ -12,6 +12,17 @@ int sa_record_cuda_error(cudaError_t e) {
   return SA_ERR_LAUNCH;
 }
 
+namespace sa {
+int norm_timeouts(int reset);  // norm.cu
+int flash_timeouts(int reset);  // flash kernels
+}  // namespace sa
+
+extern "C" int sa_device_status(int reset) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return sa_record_cuda_error(cudaGetLastError());
+  const int n = sa::norm_timeouts(reset) + sa::flash_timeouts(reset);
+  return n ? SA_ERR_TIMEOUT : SA_OK;
+}
+
 extern "C" int sa_version(void) { return (0 << 16) | 1; }
 
 extern "C" const char* sa_last_cuda_error(void) { return g_last_err; }

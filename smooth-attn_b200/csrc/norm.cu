@@ -200,6 +200,240 @@ __global__ void __launch_bounds__(512) norm_bwd_kernel(const T* __restrict__ x, 
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Bulk-copy pipelined kernels (16-byte aligned rows: the fast path)
+//
+// Every warp is an independent persistent worker with a private ring of NST
+// shared-memory row slots.  Lane 0 streams the visible bytes of the warp's
+// upcoming rows into the ring with 1-D cp.async.bulk copies (completion
+// counted on one mbarrier per slot), so up to NST rows per warp are in flight
+// without holding registers; the lanes then read the row from shared memory
+// with conflict-free 16-byte loads, reduce with warp shuffles and store the
+// full output row (zeros included) with 16-byte streaming stores.
+// ---------------------------------------------------------------------------
+
+static __device__ unsigned g_norm_timeouts;  // bounded-wait failures (never traps)
+
+constexpr int kBulkWarps = 4;     // warps per CTA
+constexpr int kMaxStages = 8;     // slots per warp (upper bound)
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Wait (bounded) on a slot; warp-uniform result.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t phase) {
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, phase));
+  if (!ok && (threadIdx.x & 31) == 0) atomicAdd(&g_norm_timeouts, 1u);
+  return ok;
+}
+
+// fwd: CH = 16-byte vectors per lane held in registers (KEEP_Y), or 0 for rows
+// too long to hold (then y is recomputed from shared memory in a second pass).
+template <typename T, int CH, bool CAUSAL>
+__global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __restrict__ x, T* __restrict__ out,
+                                                                 float* __restrict__ rowsum, int64_t rows, int cols,
+                                                                 int64_t ldx, int64_t ldo, float alpha, float theta,
+                                                                 int power, int nst, int sb) {
+  constexpr int VEC = 16 / sizeof(T);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMaxStages;
+  uint8_t* ring = smem + kBulkWarps * kMaxStages * 8 + (size_t)warp * nst * sb;
+  const int64_t nw = (int64_t)gridDim.x * kBulkWarps;
+  const int64_t first = (int64_t)blockIdx.x * kBulkWarps + warp;
+  const int nvec = cols / VEC;
+
+  auto issue = [&](int64_t row, int s) {
+    const int q = CAUSAL ? (int)(row % cols) : cols - 1;
+    const uint32_t bytes = (uint32_t)((q + VEC) / VEC) * 16u;
+    mbar_arrive_expect_tx(&bars[s], bytes);
+    bulk_g2s(ring + (size_t)s * sb, x + row * ldx, bytes, &bars[s]);
+  };
+  if (lane == 0) {
+    for (int s = 0; s < nst; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    for (int s = 0; s < nst; ++s) {
+      const int64_t r = first + s * nw;
+      if (r < rows) issue(r, s);
+    }
+  }
+  __syncwarp();
+
+  int k = 0;
+  for (int64_t row = first; row < rows; row += nw, ++k) {
+    const int s = k % nst;
+    if (!warp_wait(&bars[s], (uint32_t)(k / nst) & 1u)) return;
+    const int q = CAUSAL ? (int)(row % cols) : cols - 1;
+    const int nvis = (q + VEC) / VEC;
+    const uint8_t* slot = ring + (size_t)s * sb;
+    T* orow = out + row * ldo;
+    float sum = 0.f;
+    if constexpr (CH > 0) {
+      float y[CH][VEC];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int v = lane + 32 * c;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) y[c][e] = 0.f;
+        if (32 * c < nvis && v < nvis) {
+          Pack<T, VEC> p;
+          p.u = *reinterpret_cast<const uint4*>(slot + (size_t)v * 16);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            float yy = family_y(p.get(e), alpha, theta, power);
+            if (CAUSAL && v * VEC + e > q) yy = 0.f;
+            y[c][e] = yy;
+            sum += yy;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && row + nst * nw < rows) issue(row + nst * nw, s);  // slot consumed
+      const float S = warp_sum(sum) + SA_EPS;
+      const float inv = 1.0f / S;
+      if (rowsum != nullptr && lane == 0) rowsum[row] = S;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int v = lane + 32 * c;
+        if (v < nvec) {
+          Pack<T, VEC> o;
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o.set(e, y[c][e] * inv);
+          store_stream(orow + (int64_t)v * VEC, o);
+        }
+      }
+    } else {
+      for (int v = lane; v < nvis; v += 32) {
+        Pack<T, VEC> p;
+        p.u = *reinterpret_cast<const uint4*>(slot + (size_t)v * 16);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float yy = family_y(p.get(e), alpha, theta, power);
+          sum += (CAUSAL && v * VEC + e > q) ? 0.f : yy;
+        }
+      }
+      const float S = warp_sum(sum) + SA_EPS;
+      const float inv = 1.0f / S;
+      if (rowsum != nullptr && lane == 0) rowsum[row] = S;
+      for (int v = lane; v < nvec; v += 32) {
+        Pack<T, VEC> o;
+        if (v < nvis) {
+          Pack<T, VEC> p;
+          p.u = *reinterpret_cast<const uint4*>(slot + (size_t)v * 16);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const float yy = family_y(p.get(e), alpha, theta, power);
+            o.set(e, (CAUSAL && v * VEC + e > q) ? 0.f : yy * inv);
+          }
+        } else {
+          o.zero();
+        }
+        store_stream(orow + (int64_t)v * VEC, o);
+      }
+      __syncwarp();
+      if (lane == 0 && row + nst * nw < rows) issue(row + nst * nw, s);
+    }
+  }
+}
+
+// bwd: a slot holds the visible part of the x row followed (at offset gofs)
+// by the visible part of the g row; y is recomputed in the second pass.
+template <typename T, typename TG, bool CAUSAL>
+__global__ void __launch_bounds__(kBulkWarps * 32) norm_bwd_bulk(const T* __restrict__ x, const TG* __restrict__ g,
+                                                                 const float* __restrict__ rowsum, T* __restrict__ dx,
+                                                                 int64_t rows, int cols, int64_t ldx, int64_t ldg,
+                                                                 int64_t ldd, float alpha, float theta, int power,
+                                                                 int nst, int sb, int gofs) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int GB = VEC * (int)sizeof(TG);  // bytes of g per x vector (8, 16 or 32)
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kMaxStages;
+  uint8_t* ring = smem + kBulkWarps * kMaxStages * 8 + (size_t)warp * nst * sb;
+  const int64_t nw = (int64_t)gridDim.x * kBulkWarps;
+  const int64_t first = (int64_t)blockIdx.x * kBulkWarps + warp;
+  const int nvec = cols / VEC;
+
+  auto issue = [&](int64_t row, int s) {
+    const int q = CAUSAL ? (int)(row % cols) : cols - 1;
+    const int nv = (q + VEC) / VEC;
+    const uint32_t bx = (uint32_t)nv * 16u;
+    const uint32_t bg = ((uint32_t)nv * GB + 15u) & ~15u;  // g rows are 16 B aligned; may over-read <16 B
+    mbar_arrive_expect_tx(&bars[s], bx + bg);
+    bulk_g2s(ring + (size_t)s * sb, x + row * ldx, bx, &bars[s]);
+    bulk_g2s(ring + (size_t)s * sb + gofs, g + row * ldg, bg, &bars[s]);
+  };
+  if (lane == 0) {
+    for (int s = 0; s < nst; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    for (int s = 0; s < nst; ++s) {
+      const int64_t r = first + s * nw;
+      if (r < rows) issue(r, s);
+    }
+  }
+  __syncwarp();
+
+  const float ap = alpha * (float)power;
+  int k = 0;
+  for (int64_t row = first; row < rows; row += nw, ++k) {
+    const int s = k % nst;
+    if (!warp_wait(&bars[s], (uint32_t)(k / nst) & 1u)) return;
+    const int q = CAUSAL ? (int)(row % cols) : cols - 1;
+    const int nvis = (q + VEC) / VEC;
+    const uint8_t* sx = ring + (size_t)s * sb;
+    const TG* sg = reinterpret_cast<const TG*>(sx + gofs);
+    float sum_y = 0.f, sum_gy = 0.f;
+    for (int v = lane; v < nvis; v += 32) {
+      Pack<T, VEC> p;
+      p.u = *reinterpret_cast<const uint4*>(sx + (size_t)v * 16);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        if (!CAUSAL || v * VEC + e <= q) {
+          const float yy = family_y(p.get(e), alpha, theta, power);
+          sum_y += yy;
+          sum_gy += to_f<TG>(sg[v * VEC + e]) * yy;
+        }
+      }
+    }
+    const float S = rowsum != nullptr ? __ldg(rowsum + row) : warp_sum(sum_y) + SA_EPS;
+    const float invS = 1.0f / S;
+    const float dot = warp_sum(sum_gy) * invS;
+    T* drow = dx + row * ldd;
+    for (int v = lane; v < nvec; v += 32) {
+      Pack<T, VEC> o;
+      if (v < nvis) {
+        Pack<T, VEC> p;
+        p.u = *reinterpret_cast<const uint4*>(sx + (size_t)v * 16);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          float d = 0.f;
+          if (!CAUSAL || v * VEC + e <= q) {
+            const float a = alpha * (p.get(e) - theta);
+            const float u = fmaf(a, a, 4.0f);
+            const float r = rsqrtf(u);
+            const float sp = 0.5f * (a + u * r);
+            const float spp = 0.5f * fmaf(a, r, 1.0f);
+            float dydx = ap * spp;
+            if (power >= 2) dydx *= sp;
+            if (power == 3) dydx *= sp;
+            d = (dydx * invS) * (to_f<TG>(sg[v * VEC + e]) - dot);
+          }
+          o.set(e, d);
+        }
+      } else {
+        o.zero();
+      }
+      store_stream(drow + (int64_t)v * VEC, o);
+    }
+    __syncwarp();
+    if (lane == 0 && row + nst * nw < rows) issue(row + nst * nw, s);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -296,6 +530,108 @@ static void launch_bwd_t(int vec, bool causal, const LaunchShape& s, const void*
   }
 }
 
+
+static int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+constexpr int kWarpSmemBudget = 14 * 1024;  // ring bytes per warp (4 warps -> ~57 KB per CTA)
+
+struct BulkShape {
+  int nst, sb;
+  size_t smem;
+};
+
+static BulkShape bulk_shape(int slot_bytes) {
+  BulkShape b;
+  b.sb = (slot_bytes + 127) & ~127;
+  b.nst = kWarpSmemBudget / b.sb;
+  if (b.nst < 1) b.nst = 1;
+  if (b.nst > kMaxStages) b.nst = kMaxStages;
+  b.smem = (size_t)kBulkWarps * kMaxStages * 8 + (size_t)kBulkWarps * b.nst * b.sb;
+  return b;
+}
+
+template <typename K>
+static unsigned bulk_grid(K kernel, size_t smem, int64_t rows) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int occ = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kBulkWarps * 32, smem);
+  if (occ < 1) occ = 1;
+  const int64_t want = (rows + kBulkWarps - 1) / kBulkWarps;
+  const int64_t cap = (int64_t)sm_count() * occ;
+  return (unsigned)(want < cap ? want : cap);
+}
+
+template <typename T, int CH, bool CAUSAL>
+static void fwd_bulk_launch(const void* x, void* out, float* rowsum, int64_t rows, int cols, int64_t ldx,
+                            int64_t ldo, float alpha, float theta, int power, cudaStream_t st) {
+  const BulkShape b = bulk_shape(cols * (int)sizeof(T));
+  auto k = norm_fwd_bulk<T, CH, CAUSAL>;
+  const unsigned grid = bulk_grid(k, b.smem, rows);
+  k<<<grid, kBulkWarps * 32, b.smem, st>>>(static_cast<const T*>(x), static_cast<T*>(out), rowsum, rows, cols,
+                                            ldx, ldo, alpha, theta, power, b.nst, b.sb);
+}
+
+template <typename T, bool CAUSAL>
+static void fwd_bulk_t(const void* x, void* out, float* rowsum, int64_t rows, int cols, int64_t ldx, int64_t ldo,
+                       float alpha, float theta, int power, cudaStream_t st) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int nvec = cols / VEC;
+  const int ch = next_pow2((nvec + 31) / 32);
+#define SA_FB(CH) fwd_bulk_launch<T, CH, CAUSAL>(x, out, rowsum, rows, cols, ldx, ldo, alpha, theta, power, st)
+  if (ch * VEC > 64) { SA_FB(0); return; }
+  switch (ch) {
+    case 1: SA_FB(1); break;
+    case 2: SA_FB(2); break;
+    case 4: SA_FB(4); break;
+    case 8: SA_FB(8); break;
+    default: if constexpr (VEC <= 4) { SA_FB(16); } else { SA_FB(0); } break;
+  }
+#undef SA_FB
+}
+
+template <typename T, typename TG, bool CAUSAL>
+static void bwd_bulk_launch(const void* x, const void* g, const float* rowsum, void* dx, int64_t rows, int cols,
+                            int64_t ldx, int64_t ldg, int64_t ldd, float alpha, float theta, int power,
+                            cudaStream_t st) {
+  const int gofs = (cols * (int)sizeof(T) + 15) & ~15;
+  const int gbytes = (cols * (int)sizeof(TG) + 15) & ~15;
+  const BulkShape b = bulk_shape(gofs + gbytes);
+  auto k = norm_bwd_bulk<T, TG, CAUSAL>;
+  const unsigned grid = bulk_grid(k, b.smem, rows);
+  k<<<grid, kBulkWarps * 32, b.smem, st>>>(static_cast<const T*>(x), static_cast<const TG*>(g), rowsum,
+                                            static_cast<T*>(dx), rows, cols, ldx, ldg, ldd, alpha, theta, power,
+                                            b.nst, b.sb, gofs);
+}
+
+template <typename T, typename TG>
+static void bwd_bulk_t(bool causal, const void* x, const void* g, const float* rowsum, void* dx, int64_t rows,
+                       int cols, int64_t ldx, int64_t ldg, int64_t ldd, float alpha, float theta, int power,
+                       cudaStream_t st) {
+  if (causal) bwd_bulk_launch<T, TG, true>(x, g, rowsum, dx, rows, cols, ldx, ldg, ldd, alpha, theta, power, st);
+  else bwd_bulk_launch<T, TG, false>(x, g, rowsum, dx, rows, cols, ldx, ldg, ldd, alpha, theta, power, st);
+}
+
+int norm_timeouts(int reset) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_norm_timeouts, sizeof(v));
+  if (reset) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_norm_timeouts, &z, sizeof(z));
+  }
+  return (int)v;
+}
+
 }  // namespace sa
 
 int sa_record_cuda_error(cudaError_t e);  // defined in abi.cu
@@ -316,8 +652,21 @@ extern "C" int sa_norm_fwd(const void* x, void* out, float* rowsum, int64_t rows
   const bool vec_ok = aligned16(x) && aligned16(out) && (cols % V) == 0 && ((ld_x * es) % 16) == 0 &&
                       ((ld_out * es) % 16) == 0;
   const int vec = vec_ok ? V : 1;
-  const LaunchShape s = pick_shape(rows, (int)cols, vec, vec == 1 ? 16 : 8);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (vec_ok) {
+    const int c = (int)cols;
+#define SA_FWD_BULK(T)                                                                               \
+    if (causal) fwd_bulk_t<T, true>(x, out, rowsum, rows, c, ld_x, ld_out, alpha, theta, power, st); \
+    else fwd_bulk_t<T, false>(x, out, rowsum, rows, c, ld_x, ld_out, alpha, theta, power, st);
+    switch (dtype) {
+      case SA_F32: SA_FWD_BULK(float); break;
+      case SA_F16: SA_FWD_BULK(__half); break;
+      default: SA_FWD_BULK(__nv_bfloat16); break;
+    }
+#undef SA_FWD_BULK
+    return sa_record_cuda_error(cudaGetLastError());
+  }
+  const LaunchShape s = pick_shape(rows, (int)cols, vec, 16);
   switch (dtype) {
     case SA_F32: launch_fwd_t<float>(vec, causal, s, x, out, rowsum, rows, (int)cols, ld_x, ld_out, alpha, theta, power, st); break;
     case SA_F16: launch_fwd_t<__half>(vec, causal, s, x, out, rowsum, rows, (int)cols, ld_x, ld_out, alpha, theta, power, st); break;
@@ -341,12 +690,26 @@ extern "C" int sa_norm_bwd(const void* x, const void* g, const float* rowsum, vo
   const size_t es = dtype_size(dtype), gs = dtype_size(g_dtype);
   const int V = (int)(16 / es);
   const bool vec_ok = aligned16(x) && aligned16(dx) && aligned16(g) && (cols % V) == 0 &&
-                      ((ld_x * es) % 16) == 0 && ((ld_dx * es) % 16) == 0 && ((ld_g * gs) % 16) == 0 &&
-                      ((size_t)V * gs) % 16 == 0;
+                      ((ld_x * es) % 16) == 0 && ((ld_dx * es) % 16) == 0 && ((ld_g * gs) % 16) == 0;
   const int vec = vec_ok ? V : 1;
-  const LaunchShape s = pick_shape(rows, (int)cols, vec, vec == 1 ? 8 : 4);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int c = (int)cols;
+  if (vec_ok && ((size_t)cols * gs) % 16 == 0) {
+#define SA_BWD_BULK_G(T)                                                                                            \
+    switch (g_dtype) {                                                                                              \
+      case SA_F32: bwd_bulk_t<T, float>(causal, x, g, rowsum, dx, rows, c, ld_x, ld_g, ld_dx, alpha, theta, power, st); break; \
+      case SA_F16: bwd_bulk_t<T, __half>(causal, x, g, rowsum, dx, rows, c, ld_x, ld_g, ld_dx, alpha, theta, power, st); break; \
+      default: bwd_bulk_t<T, __nv_bfloat16>(causal, x, g, rowsum, dx, rows, c, ld_x, ld_g, ld_dx, alpha, theta, power, st); break; \
+    }
+    switch (dtype) {
+      case SA_F32: SA_BWD_BULK_G(float); break;
+      case SA_F16: SA_BWD_BULK_G(__half); break;
+      default: SA_BWD_BULK_G(__nv_bfloat16); break;
+    }
+#undef SA_BWD_BULK_G
+    return sa_record_cuda_error(cudaGetLastError());
+  }
+  const LaunchShape s = pick_shape(rows, (int)cols, vec, 8);
 #define SA_BWD_G(T)                                                                                           \
   switch (g_dtype) {                                                                                          \
     case SA_F32: launch_bwd_t<T, float>(vec, causal, s, x, g, rowsum, dx, rows, c, ld_x, ld_g, ld_dx, alpha, theta, power, st); break; \

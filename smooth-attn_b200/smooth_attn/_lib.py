@@ -35,6 +35,7 @@ SIGNATURES = {
     "sa_version": (_int, []),
     "sa_status_string": (ctypes.c_char_p, [_int]),
     "sa_last_cuda_error": (ctypes.c_char_p, []),
+    "sa_device_status": (_int, [_int]),
     "sa_norm_fwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _int, _int, _f, _f, _int, _p]),
     "sa_norm_bwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _f, _f, _int, _p]),
     "sa_flash_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,

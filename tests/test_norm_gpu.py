@@ -231,3 +231,10 @@ def test_baseline_config3_bwd_slice_and_linearity():
     y = sa.softplus_norm_causal(x)
     y.backward(g * 2)
     assert torch.equal(x.grad, gx * 2)
+
+
+def test_zz_no_device_timeouts_recorded():
+    """No bounded device-side wait of the library gave up during this module."""
+    from smooth_attn import _lib
+
+    assert _lib.load().sa_device_status(1) == _lib.SA_OK
