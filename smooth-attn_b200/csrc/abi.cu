@@ -14,12 +14,13 @@ int sa_record_cuda_error(cudaError_t e) {
 
 namespace sa {
 int norm_timeouts(int reset);  // norm.cu
-int flash_timeouts(int reset);  // flash kernels
+int flash_timeouts(int reset);      // flash_fwd.cu
+int flash_bwd_timeouts(int reset);  // flash_bwd.cu
 }  // namespace sa
 
 extern "C" int sa_device_status(int reset) {
   if (cudaDeviceSynchronize() != cudaSuccess) return sa_record_cuda_error(cudaGetLastError());
-  const int n = sa::norm_timeouts(reset) + sa::flash_timeouts(reset);
+  const int n = sa::norm_timeouts(reset) + sa::flash_timeouts(reset) + sa::flash_bwd_timeouts(reset);
   return n ? SA_ERR_TIMEOUT : SA_OK;
 }
 

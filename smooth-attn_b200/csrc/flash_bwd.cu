@@ -1,0 +1,547 @@
+// Fused causal squareplus attention, backward, on tcgen05 tensor cores.
+//
+// Reference algorithm: src/smooth_attn/kernels.py:1680-1909
+// (_sp2norm_flash_bwd_dq_kernel, _sp2norm_flash_bwd_dkv_kernel) and the host
+// wrapper :1934-1989:
+//   delta = rowsum(dO * O);  s = (q . k) * scale;  a = 2 s - 1;
+//   sp = (a + sqrt(a^2+4)) / 2;  y = sp^2;  sp' = (1 + a / sqrt(a^2+4)) / 2
+//   P = y / R;  dP = dO V^T;  dY = (dP - delta) / R;  dS = dY * 4 sp sp' * scale
+//   dQ = dS K;  dK = dS^T Q;  dV = P^T dO   (bf16 operands, fp32 accumulate)
+//
+// B200 design (three launches):
+//   1. flash_bwd_prep: delta = rowsum(dO * O) per query row (fp32) and zero
+//      the fp32 dQ accumulator (memory-bound, 16-byte vector loads);
+//   2. flash_bwd_kernel: one CTA per 128-row KV tile of one (batch, kv head),
+//      looping over the query heads of its GQA group and the 128-row query
+//      tiles that can see it.  K and V stay resident in shared memory; Q / dO
+//      tiles stream through a 2-stage TMA ring.  Per query tile:
+//        MMA   S^T = K Q^T,  dP^T = V dO^T         (TMEM, 128 cols each)
+//        warps 2..5 (thread = KV row): P -> TMEM (over S^T, bf16),
+//              dS -> shared memory (bf16, 128 B swizzle)
+//        MMA   dV += P^T dO (P from TMEM), dK += dS^T Q, dQ = dS K (into the
+//              dP^T columns)
+//        warps 2..5 (thread = query row): dQ rows -> fp32 vector atomics
+//      dK / dV accumulate in TMEM over the whole loop (GQA heads summed
+//      in-CTA like the reference) and are written once at the end.
+//   3. flash_bwd_dq_convert: dQ accumulator -> dq (bf16/fp16, caller strides).
+// The dS tile in shared memory is laid out once (rows = KV, 64-wide query
+// chunks, 128 B swizzle) and read by two MMAs with two descriptors: as a
+// K-major A for dK and as an MN-major A for dQ.
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "sa_sm100.cuh"
+
+namespace sa {
+namespace flash {
+
+using namespace sm100;
+
+static __device__ unsigned g_flash_bwd_timeouts;
+
+bool make_map_4d(CUtensorMap* map, const void* base, bool bf16, int64_t B, int64_t H, int64_t T, int64_t D,
+                 const int64_t* strides, int chunk, int rows);
+
+namespace {
+
+__device__ __forceinline__ bool b_wait(uint64_t* bar, uint32_t phase, bool& failed) {
+  if (failed) return false;
+  if (!mbar_wait(bar, phase)) {
+    failed = true;
+    atomicAdd(&g_flash_bwd_timeouts, 1u);
+    return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool b_warp_wait(uint64_t* bar, uint32_t phase, bool& failed) {
+  const bool ok = __all_sync(0xffffffffu, !failed && mbar_wait(bar, phase));
+  if (!ok) {
+    if (!failed && (threadIdx.x & 31) == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
+    failed = true;
+  }
+  return ok;
+}
+
+// Named barrier over the 128 threads of warps 2..5.
+__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+}  // namespace
+
+template <int D>
+struct BwdCfg {
+  static constexpr int BN = 128, BQ = 128;
+  static constexpr int CHUNK = D >= 64 ? 64 : D;
+  static constexpr int NCHUNK = D / CHUNK;
+  static constexpr int ROWB = CHUNK * 2;
+  static constexpr uint32_t SWZ = ROWB == 128 ? SW_128B : SW_64B;
+  static constexpr int SBO = 8 * ROWB;
+  static constexpr int TILE = 128 * D * 2;  // K, V, Q or dO tile bytes
+  static constexpr int DS_BYTES = BQ * BN * 2;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + TILE;
+  static constexpr int OFF_Q = OFF_V + TILE;  // 2 stages
+  static constexpr int OFF_DO = OFF_Q + 2 * TILE;  // 2 stages
+  static constexpr int OFF_DS = OFF_DO + 2 * TILE;
+  static constexpr int OFF_VEC = OFF_DS + DS_BYTES;  // invR[128], delta[128]
+  static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int TMEM_COLS = 512;  // S^T @0, dP^T / dQ @128, dK @256, dV @256+D
+};
+
+struct BwdParams {
+  void* dk;
+  void* dv;
+  const float* rowsum;  // R  [B, Hq, T]
+  const float* delta;   // [B, Hq, T]
+  float* dq_acc;        // [B, Hq, T, D] fp32
+  int64_t sdk_b, sdk_h, sdk_s;
+  int64_t sdv_b, sdv_h, sdv_s;
+  int B, Hq, Hkv, T, window;
+  float scale;
+};
+
+struct BwdBars {
+  uint64_t kv_full;
+  uint64_t qdo_full[2];
+  uint64_t qdo_empty[2];
+  uint64_t s_full;
+  uint64_t ds_ready;
+  uint64_t mm2_done;
+  uint64_t dq_free;
+  uint64_t all_done;
+  uint32_t tmem_base;
+};
+
+template <int D, bool BF16, bool EXACT>
+__global__ void __launch_bounds__(192, 1)
+    flash_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                     const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
+                     BwdParams p) {
+  using C = BwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sDO = smem + C::OFF_DO;
+  uint8_t* sDS = smem + C::OFF_DS;
+  float* sInvR = reinterpret_cast<float*>(smem + C::OFF_VEC);
+  float* sDelta = sInvR + 128;
+  BwdBars* bars = reinterpret_cast<BwdBars*>(smem + C::OFF_BAR);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * C::BN;
+  const int b = blockIdx.y / p.Hkv, kvh = blockIdx.y % p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  const int nqt = (p.T + C::BQ - 1) / C::BQ;
+  const int qt_first = n0 / C::BQ;
+  int qt_last = nqt - 1;
+  if (p.window > 0) {
+    const int last_q = n0 + C::BN - 1 + p.window - 1;
+    const int l = last_q / C::BQ;
+    if (l < qt_last) qt_last = l;
+  }
+  const int per_head = qt_last - qt_first + 1;
+  const int ntiles = G * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->qdo_full[i], 1);
+      mbar_init(&bars->qdo_empty[i], 1);
+    }
+    mbar_init(&bars->s_full, 1);
+    mbar_init(&bars->ds_ready, 128);
+    mbar_init(&bars->mm2_done, 1);
+    mbar_init(&bars->dq_free, 128);
+    mbar_init(&bars->all_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  bool failed = false;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      tma_prefetch_desc(&tmdo);
+      mbar_arrive_expect_tx(&bars->kv_full, 2 * C::TILE);
+      for (int c = 0; c < C::NCHUNK; ++c) {
+        tma_load_4d(sK + c * 128 * C::ROWB, &tmk, c * C::CHUNK, n0, kvh, b, &bars->kv_full);
+        tma_load_4d(sV + c * 128 * C::ROWB, &tmv, c * C::CHUNK, n0, kvh, b, &bars->kv_full);
+      }
+      for (int it = 0; it < ntiles; ++it) {
+        const int st = it & 1;
+        if (it >= 2 && !b_wait(&bars->qdo_empty[st], ((it >> 1) - 1) & 1, failed)) break;
+        const int h = kvh * G + it / per_head;
+        const int q0 = (qt_first + it % per_head) * C::BQ;
+        mbar_arrive_expect_tx(&bars->qdo_full[st], 2 * C::TILE);
+        for (int c = 0; c < C::NCHUNK; ++c) {
+          tma_load_4d(sQ + st * C::TILE + c * 128 * C::ROWB, &tmq, c * C::CHUNK, q0, h, b, &bars->qdo_full[st]);
+          tma_load_4d(sDO + st * C::TILE + c * 128 * C::ROWB, &tmdo, c * C::CHUNK, q0, h, b, &bars->qdo_full[st]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr int ab = BF16 ? 1 : 0;
+      constexpr uint32_t id_s = idesc_f16(128, C::BQ, ab, 0, 0);   // S^T, dP^T: A K-major, B K-major
+      constexpr uint32_t id_kv = idesc_f16(128, D, ab, 0, 1);      // dV, dK: B (dO / Q) MN-major
+      constexpr uint32_t id_dq = idesc_f16(128, D, ab, 1, 1);      // dQ: A (dS) MN-major, B (K) MN-major
+      const uint32_t tS = tbase, tP = tbase + 128, tDK = tbase + 256, tDV = tbase + 256 + D;
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
+      const uint32_t aDS = smem_u32(sDS);
+      if (b_wait(&bars->kv_full, 0, failed)) {
+        for (int it = 0; it < ntiles; ++it) {
+          const int st = it & 1;
+          if (!b_wait(&bars->qdo_full[st], (it >> 1) & 1, failed)) break;
+          if (it > 0 && !b_wait(&bars->dq_free, (it - 1) & 1, failed)) break;
+          tc_fence_after();
+          const uint32_t q_s = aQ + st * C::TILE, do_s = aDO + st * C::TILE;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int c = (kk * 16) / C::CHUNK;
+            const uint32_t off = c * 128 * C::ROWB + ((kk * 16) % C::CHUNK) * 2;
+            mma_ss(tS, smem_desc(aK + off, 16, C::SBO, C::SWZ), smem_desc(q_s + off, 16, C::SBO, C::SWZ), id_s, kk > 0);
+            mma_ss(tP, smem_desc(aV + off, 16, C::SBO, C::SWZ), smem_desc(do_s + off, 16, C::SBO, C::SWZ), id_s, kk > 0);
+          }
+          mma_commit(&bars->s_full);
+          if (!b_wait(&bars->ds_ready, it & 1, failed)) break;
+          tc_fence_after();
+          // dV += P^T dO ; dK += dS^T Q   (K = 128 query rows, 8 steps of 16)
+#pragma unroll
+          for (int kk = 0; kk < C::BQ / 16; ++kk) {
+            const uint64_t b_do = smem_desc(do_s + kk * 16 * C::ROWB, 128 * C::ROWB, C::SBO, C::SWZ);
+            const uint64_t b_q = smem_desc(q_s + kk * 16 * C::ROWB, 128 * C::ROWB, C::SBO, C::SWZ);
+            const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+            mma_ts(tDV, tS + kk * 8, b_do, id_kv, acc);
+            // dS^T as K-major A: rows = KV, 64-wide query chunks of 128 B
+            const uint64_t a_ds = smem_desc(aDS + (kk / 4) * (128 * 128) + (kk % 4) * 32, 16, 1024, SW_128B);
+            mma_ss(tDK, a_ds, b_q, id_kv, acc);
+          }
+          // dQ = dS K   (M = query rows, K = 128 KV rows)
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk) {
+            const uint64_t a_ds = smem_desc(aDS + kk * 16 * 128, 128 * 128, 1024, SW_128B);
+            const uint64_t b_k = smem_desc(aK + kk * 16 * C::ROWB, 128 * C::ROWB, C::SBO, C::SWZ);
+            mma_ss(tP, a_ds, b_k, id_dq, kk > 0);
+          }
+          mma_commit(&bars->mm2_done);
+          mma_commit(&bars->qdo_empty[st]);
+        }
+      }
+      mma_commit(&bars->all_done);
+    }
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int g = warp & 3;
+    const int r = 32 * g + lane;  // TMEM lane: KV row for S/dP/dK/dV, query row for dQ
+    const int tid = threadIdx.x - 64;
+    const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
+    const int n = n0 + r;
+    const float scale2 = 2.0f * p.scale, c4s = 4.0f * p.scale;
+    for (int it = 0; it < ntiles && !failed; ++it) {
+      const int h = kvh * G + it / per_head;
+      const int q0 = (qt_first + it % per_head) * C::BQ;
+      const int64_t rbase = ((int64_t)b * p.Hq + h) * p.T;
+      compute_sync();  // everyone done with the previous tile's invR / delta
+      {
+        const int qq = q0 + tid;
+        const bool ok = qq < p.T;
+        sInvR[tid] = ok ? 1.0f / p.rowsum[rbase + qq] : 0.f;
+        sDelta[tid] = ok ? p.delta[rbase + qq] : 0.f;
+      }
+      compute_sync();
+      if (!b_warp_wait(&bars->s_full, it & 1, failed)) break;
+      tc_fence_after();
+      const bool need_mask = (q0 < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.T) ||
+                             (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
+#pragma unroll 1
+      for (int c = 0; c < C::BQ / 32; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tl + c * 32, sv);
+        tmem_ld32(tl + 128 + c * 32, dv);
+        tmem_ld_wait();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int m = c * 32 + e + u;
+            const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
+            const float w = fmaf(a, a, 4.0f);
+            const float rs = rsqrtf(w);
+            const float sq = EXACT ? sqrtf(w) : w * rs;
+            const float sp = 0.5f * (a + sq);
+            const float spp = 0.5f * fmaf(a, rs, 1.0f);
+            const float invR = sInvR[m];
+            float pp = sp * sp * invR;
+            float ds = (__uint_as_float(dv[e + u]) - sDelta[m]) * invR * (c4s * sp * spp);
+            if (need_mask) {
+              const int q = q0 + m;
+              const bool ok = (n <= q) && (q < p.T) && (n < p.T) && (p.window <= 0 || q - n < p.window);
+              pp = ok ? pp : 0.f;
+              ds = ok ? ds : 0.f;
+            }
+            pv[u] = pp;
+            dsv[u] = ds;
+          }
+          pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
+          dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
+        }
+        tmem_st16(tl + c * 16, pk);
+        // dS row r, query columns [32c, 32c+32): chunk c/2 of 64, 16 B pieces (c%2)*4 .. +3, swizzled
+        uint8_t* row = sDS + (c >> 1) * (128 * 128) + r * 128;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int piece = ((c & 1) * 4 + j) ^ (r & 7);
+          *reinterpret_cast<uint4*>(row + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+        }
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->ds_ready);
+      // drain dQ (TMEM lane = query row) with fp32 vector atomics
+      if (!b_warp_wait(&bars->mm2_done, it & 1, failed)) break;
+      tc_fence_after();
+      const int q = q0 + r;
+      float4* dst = reinterpret_cast<float4*>(p.dq_acc + (rbase + q) * D);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tl + 128 + c * 32, v);
+        tmem_ld_wait();
+        if (q < p.T) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            atomicAdd(dst + c * 8 + j, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                   __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->dq_free);
+    }
+    // epilogue: dK, dV rows (TMEM lane = KV row)
+    if (b_warp_wait(&bars->all_done, 0, failed)) {
+      tc_fence_after();
+      const bool live = n < p.T;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        uint8_t* base = static_cast<uint8_t*>(which ? p.dv : p.dk) +
+                        2 * (which ? ((int64_t)b * p.sdv_b + (int64_t)kvh * p.sdv_h + (int64_t)n * p.sdv_s)
+                                   : ((int64_t)b * p.sdk_b + (int64_t)kvh * p.sdk_h + (int64_t)n * p.sdk_s));
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tl + 256 + which * D + c * 32, v);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            pk[e / 2] = BF16 ? pack2_bf16(__uint_as_float(v[e]), __uint_as_float(v[e + 1]))
+                             : pack2_f16(__uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+          if (live) {
+            uint4* dst = reinterpret_cast<uint4*>(base + c * 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::TMEM_COLS);
+  }
+}
+
+// delta = rowsum(dO * O) (fp32) and dq_acc = 0.  One warp per query row.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) flash_bwd_prep(const T* __restrict__ o, const T* __restrict__ dout,
+                                                      float* __restrict__ delta, float* __restrict__ dq_acc,
+                                                      int64_t rows, int Hq, int Tlen, int64_t so_b, int64_t so_h,
+                                                      int64_t so_s, int64_t sd_b, int64_t sd_h, int64_t sd_s) {
+  constexpr int VEC = 8;  // 16 bytes of 16-bit elements
+  constexpr int NV = D / VEC;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int t = (int)(row % Tlen);
+  const int64_t bh = row / Tlen;
+  const int b = (int)(bh / Hq), h = (int)(bh % Hq);
+  const T* orow = o + (int64_t)b * so_b + (int64_t)h * so_h + (int64_t)t * so_s;
+  const T* drow = dout + (int64_t)b * sd_b + (int64_t)h * sd_h + (int64_t)t * sd_s;
+  float acc = 0.f;
+  if (lane < NV) {
+    Pack<T, VEC> a, c;
+    a.u = *reinterpret_cast<const uint4*>(orow + lane * VEC);
+    c.u = *reinterpret_cast<const uint4*>(drow + lane * VEC);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc += a.get(e) * c.get(e);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) delta[row] = acc;
+  float4* z = reinterpret_cast<float4*>(dq_acc + row * D);
+  for (int i = lane; i < D / 4; i += 32) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256) flash_bwd_dq_convert(const float* __restrict__ dq_acc, T* __restrict__ dq,
+                                                            int64_t rows, int Hq, int Tlen, int64_t s_b, int64_t s_h,
+                                                            int64_t s_s) {
+  constexpr int VEC = 8;
+  constexpr int NV = D / VEC;  // vectors per row
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = idx / NV;
+  const int v = (int)(idx % NV);
+  if (row >= rows) return;
+  const int t = (int)(row % Tlen);
+  const int64_t bh = row / Tlen;
+  const int b = (int)(bh / Hq), h = (int)(bh % Hq);
+  const float4* src = reinterpret_cast<const float4*>(dq_acc + row * D + v * VEC);
+  const float4 a = src[0], c = src[1];
+  Pack<T, VEC> out;
+  out.set(0, a.x); out.set(1, a.y); out.set(2, a.z); out.set(3, a.w);
+  out.set(4, c.x); out.set(5, c.y); out.set(6, c.z); out.set(7, c.w);
+  *reinterpret_cast<uint4*>(dq + (int64_t)b * s_b + (int64_t)h * s_h + (int64_t)t * s_s + v * VEC) = out.u;
+}
+
+template <int D, bool BF16, bool EXACT>
+static int launch_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                      const float* rowsum, void* dq, void* dk, void* dv, float* dq_acc, float* delta, int64_t B,
+                      int64_t Hq, int64_t Hkv, int64_t T, const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                      const int64_t* os, const int64_t* dos, const int64_t* dqs, const int64_t* dks,
+                      const int64_t* dvs, float scale, int64_t window, cudaStream_t st) {
+  using C = BwdCfg<D>;
+  using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const int64_t rows = B * Hq * T;
+  flash_bwd_prep<T16, D><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+      static_cast<const T16*>(o), static_cast<const T16*>(dout), delta, dq_acc, rows, (int)Hq, (int)T, os[0], os[1],
+      os[2], dos[0], dos[1], dos[2]);
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_map_4d(&mq, q, BF16, B, Hq, T, D, qs, C::CHUNK, C::BQ) ||
+      !make_map_4d(&mk, k, BF16, B, Hkv, T, D, ks, C::CHUNK, C::BN) ||
+      !make_map_4d(&mv, v, BF16, B, Hkv, T, D, vs, C::CHUNK, C::BN) ||
+      !make_map_4d(&mdo, dout, BF16, B, Hq, T, D, dos, C::CHUNK, C::BQ))
+    return SA_ERR_ALIGN;
+  BwdParams p;
+  p.dk = dk;
+  p.dv = dv;
+  p.rowsum = rowsum;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.sdk_b = dks[0]; p.sdk_h = dks[1]; p.sdk_s = dks[2];
+  p.sdv_b = dvs[0]; p.sdv_h = dvs[1]; p.sdv_s = dvs[2];
+  p.B = (int)B;
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.T = (int)T;
+  p.window = (int)window;
+  p.scale = scale;
+  auto kern = flash_bwd_kernel<D, BF16, EXACT>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  dim3 grid((unsigned)((T + C::BN - 1) / C::BN), (unsigned)(B * Hkv));
+  kern<<<grid, 192, C::SMEM, st>>>(mq, mk, mv, mdo, p);
+  const int64_t nthreads = rows * (D / 8);
+  flash_bwd_dq_convert<T16, D><<<(unsigned)((nthreads + 255) / 256), 256, 0, st>>>(
+      dq_acc, static_cast<T16*>(dq), rows, (int)Hq, (int)T, dqs[0], dqs[1], dqs[2]);
+  return SA_OK;
+}
+
+}  // namespace flash
+
+int flash_bwd_timeouts(int reset) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, flash::g_flash_bwd_timeouts, sizeof(v));
+  if (reset) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(flash::g_flash_bwd_timeouts, &z, sizeof(z));
+  }
+  return (int)v;
+}
+
+}  // namespace sa
+
+int sa_record_cuda_error(cudaError_t e);
+
+static bool bwd_strides_ok(const int64_t* s) {
+  return s != nullptr && s[3] == 1 && s[0] % 8 == 0 && s[1] % 8 == 0 && s[2] % 8 == 0 && s[0] >= 0 && s[1] >= 0 &&
+         s[2] > 0;
+}
+
+static int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
+
+extern "C" int64_t sa_flash_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D) {
+  (void)Hkv;
+  if (B <= 0 || Hq <= 0 || T <= 0 || D <= 0) return 0;
+  return align256(B * Hq * T * D * 4) + align256(B * Hq * T * 4);
+}
+
+extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                            const float* rowsum, void* dq, void* dk, void* dv, void* workspace,
+                            int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D,
+                            const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                            const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
+                            const int64_t* dk_strides, const int64_t* dv_strides, float scale, int64_t window_size,
+                            int exact_math, int dtype, void* stream) {
+  if (dtype != SA_BF16 && dtype != SA_F16) return SA_ERR_UNSUPPORTED;
+  if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
+  if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Hq % Hkv != 0 || window_size < 0) return SA_ERR_ARG;
+  if (B == 0 || T == 0) return SA_OK;
+  if (T > (1ll << 30) || B * Hkv > 65535) return SA_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !o || !dout || !rowsum || !dq || !dk || !dv || !workspace) return SA_ERR_ARG;
+  if (workspace_bytes < sa_flash_bwd_workspace_size(B, Hq, Hkv, T, D)) return SA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_ALIGN;
+  const int64_t* all[8] = {q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides};
+  for (auto s : all)
+    if (!bwd_strides_ok(s)) return SA_ERR_ALIGN;
+  const void* ptrs[9] = {q, k, v, o, dout, dq, dk, dv, rowsum};
+  for (auto p : ptrs)
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return SA_ERR_ALIGN;
+  float* dq_acc = static_cast<float*>(workspace);
+  float* delta = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(B * Hq * T * D * 4));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using namespace sa::flash;
+  int rc;
+#define SA_BWD_CASE(DD, BF, EX)                                                                                  \
+  rc = launch_bwd<DD, BF, EX>(q, k, v, o, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, T, q_strides,     \
+                              k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, \
+                              scale, window_size, st)
+#define SA_BWD_D(DD)                              \
+  if (dtype == SA_BF16) {                         \
+    if (exact_math) SA_BWD_CASE(DD, true, true);  \
+    else SA_BWD_CASE(DD, true, false);            \
+  } else {                                        \
+    if (exact_math) SA_BWD_CASE(DD, false, true); \
+    else SA_BWD_CASE(DD, false, false);           \
+  }
+  if (D == 32) {
+    SA_BWD_D(32)
+  } else if (D == 64) {
+    SA_BWD_D(64)
+  } else {
+    SA_BWD_D(128)
+  }
+#undef SA_BWD_D
+#undef SA_BWD_CASE
+  if (rc != SA_OK) return rc;
+  return sa_record_cuda_error(cudaGetLastError());
+}

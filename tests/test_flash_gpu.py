@@ -144,3 +144,99 @@ def test_zz_flash_no_device_timeouts():
     from smooth_attn import _lib
 
     assert _lib.load().sa_device_status(1) == _lib.SA_OK
+
+
+# ---- backward --------------------------------------------------------------
+
+
+def _bwd_case(B, Hq, Hkv, T, D, W=0, seed=0, exact=False, dtype=torch.bfloat16, noncontig=False):
+    if noncontig:
+        q = randn((B, T, Hq, D), seed, dtype, CUDA).transpose(1, 2)
+        k = randn((B, T, Hkv, D), seed + 1, dtype, CUDA).transpose(1, 2)
+        v = randn((B, T, Hkv, D), seed + 2, dtype, CUDA).transpose(1, 2)
+    else:
+        q, k, v = _qkv(B, Hq, Hkv, T, D, seed, dtype)
+    q, k, v = (t.detach().requires_grad_(True) for t in (q, k, v))
+    do = randn((B, Hq, T, D), seed + 3, torch.float32, CUDA)
+    o = sa.sp2norm_flash_attention(q, k, v, window_size=W, exact_math=exact)
+    (o.float() * do).sum().backward()
+    dq, dk, dv = O.sp2norm_flash_attention_bwd(np32(q), np32(k), np32(v), np32(do.to(dtype)), window_size=W)
+    for got, ref in ((q.grad, dq), (k.grad, dk), (v.grad, dv)):
+        assert got.dtype == dtype and got.shape == ref.shape
+        assert torch.isfinite(got.float()).all()
+        assert_close(np32(got), ref, **BWD_TOL)
+
+
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("T", [1, 5, 64, 128, 129, 257])
+def test_flash_bwd_matches_oracle(D, T):
+    _bwd_case(1, 2, 2, T, D, seed=T * 7 + D)
+
+
+def test_flash_backward_reference_case():
+    """reference tests/test_training_api.py:128-154 (eager softplus-norm on explicit scores)."""
+    B, H, T, D = 1, 2, 64, 32
+    scale = 1.0 / (D ** 0.5)
+    q, k, v = (t.requires_grad_(True) for t in _qkv(B, H, H, T, D, seed=21))
+    upstream = randn((B, H, T, D), 24, torch.float32, CUDA)
+    (sa.sp2norm_flash_attention(q, k, v).float() * upstream).sum().backward()
+    qr, kr, vr = (t.detach().clone().float().requires_grad_(True) for t in (q, k, v))
+    attn = sa.softplus_norm_causal_eager(torch.matmul(qr, kr.transpose(-2, -1)) * scale)
+    (torch.matmul(attn, vr) * upstream).sum().backward()
+    for got, ref in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
+        torch.testing.assert_close(got.float(), ref.float(), atol=5e-2, rtol=0.1)
+
+
+def test_flash_bwd_exact_math():
+    _bwd_case(1, 2, 2, 64, 32, seed=31, exact=True)
+
+
+@pytest.mark.parametrize(("Hq", "Hkv"), [(8, 2), (8, 4), (4, 1)])
+def test_flash_bwd_gqa(Hq, Hkv):
+    _bwd_case(1, Hq, Hkv, 64, 32, seed=40 + Hq + Hkv)
+    _bwd_case(1, Hq, Hkv, 200, 64, seed=50 + Hq + Hkv)
+
+
+@pytest.mark.parametrize("W", [32, 64, 130])
+def test_flash_bwd_window(W):
+    _bwd_case(1, 2, 2, 128, 32, W=W, seed=60 + W)
+    _bwd_case(1, 2, 2, 300, 128, W=W, seed=70 + W)
+
+
+def test_flash_bwd_gqa_window_noncontiguous():
+    _bwd_case(1, 8, 2, 64, 32, W=32, seed=80)
+    _bwd_case(1, 8, 2, 64, 32, W=32, seed=81, noncontig=True)
+
+
+def test_flash_bwd_fp16():
+    _bwd_case(1, 2, 2, 160, 64, seed=90, dtype=torch.float16)
+
+
+@pytest.mark.parametrize("name", sorted({k.split("/")[0] for k in G.files if k.startswith("f_")}))
+def test_flash_golden_bwd(name):
+    q, k, v = (torch.from_numpy(G[f"{name}/{s}"]).to(torch.bfloat16).to(CUDA).requires_grad_(True)
+               for s in ("q", "k", "v"))
+    do = torch.from_numpy(G[f"{name}/do"]).to(CUDA)
+    w = int(G[f"{name}/window"])
+    (sa.sp2norm_flash_attention(q, k, v, window_size=w).float() * do).sum().backward()
+    for t, s in ((q, "dq"), (k, "dk"), (v, "dv")):
+        assert_close(np32(t.grad), G[f"{name}/{s}"], **BWD_TOL)
+
+
+def test_flash_bwd_baseline_config4_slices():
+    """[4,32,4096,128] fwd+bwd: sampled heads equal the oracle."""
+    B, H, T, D = 4, 32, 4096, 128
+    q, k, v = (t.requires_grad_(True) for t in _qkv(B, H, H, T, D, seed=444))
+    do = randn((B, H, T, D), 448, torch.bfloat16, CUDA)
+    sa.sp2norm_flash_attention(q, k, v).backward(do)
+    for b, h in ((0, 5), (3, 31)):
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        dq, dk, dv = O.sp2norm_flash_attention_bwd(np32(q[sl]), np32(k[sl]), np32(v[sl]), np32(do[sl]))
+        for got, ref in ((q.grad[sl], dq), (k.grad[sl], dk), (v.grad[sl], dv)):
+            assert_close(np32(got), ref, **BWD_TOL)
+
+
+def test_zzz_flash_bwd_no_device_timeouts():
+    from smooth_attn import _lib
+
+    assert _lib.load().sa_device_status(1) == _lib.SA_OK
