@@ -69,6 +69,54 @@ __device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 128;"
 
 }  // namespace
 
+// One 32-column chunk (query columns [32c, 32c+32)) of the backward
+// elementwise stage for the KV row held by this thread: P -> TMEM (over S^T),
+// dS -> the swizzled shared-memory tile.
+template <bool BF16, bool EXACT, bool MASK>
+__device__ __forceinline__ void bwd_chunk(uint32_t tl, int c, uint8_t* sDS, int r, const float* sInvR,
+                                          const float* sDelta, float scale2, float c4s, int n, int q0, int T,
+                                          int window) {
+  uint32_t sv[32], dv[32];
+  tmem_ld32(tl + c * 32, sv);
+  tmem_ld32(tl + 128 + c * 32, dv);
+  tmem_ld_wait();
+  uint32_t pk[16], dk[16];
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    float pv[2], dsv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int m = c * 32 + e + u;
+      const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
+      const float w = fmaf(a, a, 4.0f);
+      const float rs = rsqrtf(w);
+      const float sq = EXACT ? sqrtf(w) : w * rs;
+      const float sp = 0.5f * (a + sq);
+      const float spp = 0.5f * fmaf(a, rs, 1.0f);
+      const float invR = sInvR[m];
+      float pp = sp * sp * invR;
+      float ds = (__uint_as_float(dv[e + u]) - sDelta[m]) * invR * (c4s * sp * spp);
+      if (MASK) {
+        const int q = q0 + m;
+        const bool ok = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
+        pp = ok ? pp : 0.f;
+        ds = ok ? ds : 0.f;
+      }
+      pv[u] = pp;
+      dsv[u] = ds;
+    }
+    pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
+    dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
+  }
+  tmem_st16(tl + c * 16, pk);
+  uint8_t* row = sDS + (c >> 1) * (128 * 128) + r * 128;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int piece = ((c & 1) * 4 + j) ^ (r & 7);
+    *reinterpret_cast<uint4*>(row + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+  }
+}
+
 template <int D>
 struct BwdCfg {
   static constexpr int BN = 128, BQ = 128;
@@ -252,64 +300,39 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     const int n = n0 + r;
     const float scale2 = 2.0f * p.scale, c4s = 4.0f * p.scale;
+    // R^-1 and delta of the next query tile are prefetched into registers one
+    // tile ahead, so their global-load latency hides behind the current tile.
+    float pre_invR = 0.f, pre_delta = 0.f;
+    auto prefetch = [&](int it) {
+      const int h = kvh * G + it / per_head;
+      const int qq = (qt_first + it % per_head) * C::BQ + tid;
+      const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + qq;
+      const bool ok = it < ntiles && qq < p.T;
+      pre_invR = ok ? 1.0f / __ldg(p.rowsum + idx) : 0.f;
+      pre_delta = ok ? __ldg(p.delta + idx) : 0.f;
+    };
+    prefetch(0);
     for (int it = 0; it < ntiles && !failed; ++it) {
       const int h = kvh * G + it / per_head;
       const int q0 = (qt_first + it % per_head) * C::BQ;
       const int64_t rbase = ((int64_t)b * p.Hq + h) * p.T;
       compute_sync();  // everyone done with the previous tile's invR / delta
-      {
-        const int qq = q0 + tid;
-        const bool ok = qq < p.T;
-        sInvR[tid] = ok ? 1.0f / p.rowsum[rbase + qq] : 0.f;
-        sDelta[tid] = ok ? p.delta[rbase + qq] : 0.f;
-      }
+      sInvR[tid] = pre_invR;
+      sDelta[tid] = pre_delta;
       compute_sync();
+      prefetch(it + 1);
       if (!b_warp_wait(&bars->s_full, it & 1, failed)) break;
       tc_fence_after();
       const bool need_mask = (q0 < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.T) ||
                              (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
+      if (need_mask) {
 #pragma unroll 1
-      for (int c = 0; c < C::BQ / 32; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tl + c * 32, sv);
-        tmem_ld32(tl + 128 + c * 32, dv);
-        tmem_ld_wait();
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int m = c * 32 + e + u;
-            const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
-            const float w = fmaf(a, a, 4.0f);
-            const float rs = rsqrtf(w);
-            const float sq = EXACT ? sqrtf(w) : w * rs;
-            const float sp = 0.5f * (a + sq);
-            const float spp = 0.5f * fmaf(a, rs, 1.0f);
-            const float invR = sInvR[m];
-            float pp = sp * sp * invR;
-            float ds = (__uint_as_float(dv[e + u]) - sDelta[m]) * invR * (c4s * sp * spp);
-            if (need_mask) {
-              const int q = q0 + m;
-              const bool ok = (n <= q) && (q < p.T) && (n < p.T) && (p.window <= 0 || q - n < p.window);
-              pp = ok ? pp : 0.f;
-              ds = ok ? ds : 0.f;
-            }
-            pv[u] = pp;
-            dsv[u] = ds;
-          }
-          pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
-          dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
-        }
-        tmem_st16(tl + c * 16, pk);
-        // dS row r, query columns [32c, 32c+32): chunk c/2 of 64, 16 B pieces (c%2)*4 .. +3, swizzled
-        uint8_t* row = sDS + (c >> 1) * (128 * 128) + r * 128;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int piece = ((c & 1) * 4 + j) ^ (r & 7);
-          *reinterpret_cast<uint4*>(row + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
-        }
+        for (int c = 0; c < C::BQ / 32; ++c)
+          bwd_chunk<BF16, EXACT, true>(tl, c, sDS, r, sInvR, sDelta, scale2, c4s, n, q0, p.T, p.window);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < C::BQ / 32; ++c)
+          bwd_chunk<BF16, EXACT, false>(tl, c, sDS, r, sInvR, sDelta, scale2, c4s, n, q0, p.T, p.window);
       }
       tmem_st_wait();
       fence_proxy_async_smem();

@@ -39,41 +39,40 @@ __device__ unsigned g_flash_timeouts;
 
 template <int D>
 struct FwdCfg {
-  static constexpr int BM = 128, BN = 128;
+  static constexpr int BM = 128, BN = 128;  // rows per Q tile, rows per KV tile
   static constexpr int CHUNK = D >= 64 ? 64 : D;  // elements per swizzled smem row
   static constexpr int NCHUNK = D / CHUNK;
   static constexpr int ROWB = CHUNK * 2;  // bytes per smem row
   static constexpr uint32_t SWZ = ROWB == 128 ? SW_128B : SW_64B;
   static constexpr int SBO = 8 * ROWB;  // stride between 8-row groups
-  static constexpr int Q_BYTES = BM * D * 2;
-  static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int NS = D == 128 ? 2 : (D == 64 ? 3 : 4);
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + NS * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_V + NS * KV_BYTES;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + barriers + alignment slack
-  static constexpr int TMEM_COLS = 512;            // S0 @0, S1 @128, O @256
-  static constexpr int THREADS = 192;
+  static constexpr int TILE = 128 * D * 2;  // one Q, K or V tile
+  static constexpr int NK = D == 128 ? 2 : (D == 64 ? 3 : 4);  // K ring
+  static constexpr int NV = NK;                                  // V ring
+  static constexpr int OFF_Q = 0;  // Q tile A, Q tile B
+  static constexpr int OFF_K = OFF_Q + 2 * TILE;
+  static constexpr int OFF_V = OFF_K + NK * TILE;
+  static constexpr int OFF_BAR = OFF_V + NV * TILE;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;  // + barriers + alignment slack
+  static constexpr int TMEM_COLS = 512;            // S_A @0, S_B @128, O_A @256, O_B @256+D
+  static constexpr int THREADS = 320;              // WG A (w0-3), WG B (w4-7), TMA (w8), MMA (w9)
 };
 
 struct FwdParams {
   void* o;
   float* rowsum;
   int64_t so_b, so_h, so_s;
-  int B, Hq, Hkv, T, nqt, window;
+  int B, Hq, Hkv, T, npairs, window;
   float scale2;  // 2 * scale
 };
 
 struct Bars {
   uint64_t q_full;
-  uint64_t o_full;
-  uint64_t s_full[2];
-  uint64_t s_free[2];
-  uint64_t p_full[2];
-  uint64_t k_full[4];
-  uint64_t v_full[4];
-  uint64_t kv_empty[4];
+  uint64_t s_full[2];   // per Q tile: S ready in TMEM
+  uint64_t p_full[2];   // per Q tile: P written back (128 arrivals)
+  uint64_t pv_done[2];  // per Q tile: P consumed by the PV MMA
+  uint64_t o_full[2];   // per Q tile: final O in TMEM
+  uint64_t k_full[4], k_empty[4];
+  uint64_t v_full[4], v_empty[4];
   uint32_t tmem_base;
 };
 
@@ -97,8 +96,54 @@ __device__ __forceinline__ bool warp_wait_or_flag(uint64_t* bar, uint32_t phase,
   return ok;
 }
 
+// KV tile range [j0, j1) seen by the 128 query rows starting at q0.
+__device__ __forceinline__ void kv_range(int q0, int T, int window, int& j0, int& j1) {
+  const int nkv = (T + 127) / 128;
+  j1 = (q0 + 128 + 127) / 128;
+  if (j1 > nkv) j1 = nkv;
+  j0 = 0;
+  if (window > 0) {
+    const int first = q0 - window + 1;
+    j0 = first > 0 ? first / 128 : 0;
+  }
+  if (q0 >= T) j1 = j0;  // tile wholly past the sequence end: no work
+}
+
+// One 32-column chunk of squareplus on a score row held in TMEM; writes the
+// bf16/f16 P back over the chunk's first 16 columns and returns sum(y').
+template <bool BF16, bool EXACT, bool MASK>
+__device__ __forceinline__ float squareplus_chunk(uint32_t taddr_s, uint32_t taddr_p, float scale2, int kbase, int q,
+                                                  int T, int window) {
+  uint32_t r[32];
+  tmem_ld32(taddr_s, r);
+  tmem_ld_wait();
+  uint32_t pk[16];
+  float sum = 0.f;
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    float yv[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float a = fmaf(__uint_as_float(r[e + u]), scale2, -1.0f);
+      const float w = fmaf(a, a, 4.0f);
+      const float t = EXACT ? a + sqrtf(w) : fmaf(w, rsqrtf(w), a);
+      float y = t * t;  // 4 * squareplus(a)^2
+      if (MASK) {
+        const int k = kbase + e + u;
+        const bool ok = (k <= q) && (k < T) && (window <= 0 || q - k < window);
+        y = ok ? y : 0.f;
+      }
+      yv[u] = y;
+    }
+    sum += yv[0] + yv[1];
+    pk[e / 2] = BF16 ? pack2_bf16(yv[0], yv[1]) : pack2_f16(yv[0], yv[1]);
+  }
+  tmem_st16(taddr_p, pk);
+  return sum;
+}
+
 template <int D, bool BF16, bool EXACT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, FwdParams p) {
   using C = FwdCfg<D>;
@@ -110,37 +155,36 @@ __global__ void __launch_bounds__(192, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + C::OFF_BAR);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.nqt - 1 - (int)blockIdx.x;  // longest (most KV tiles) first
+  const int pair = p.npairs - 1 - (int)blockIdx.x;  // longest (most KV tiles) first
   const int bh = blockIdx.y;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvh = h / (p.Hq / p.Hkv);
-  const int q0 = qt * C::BM;
-  const int nkv_total = (p.T + C::BN - 1) / C::BN;
-  int j1 = (q0 + C::BM + C::BN - 1) / C::BN;
-  if (j1 > nkv_total) j1 = nkv_total;
-  int j0 = 0;
-  if (p.window > 0) {
-    const int first = q0 - p.window + 1;
-    j0 = first > 0 ? first / C::BN : 0;
-  }
-  const int n = j1 - j0;
+  const int qbase = pair * 2 * C::BM;
+  // per Q tile KV ranges; the CTA streams the union
+  int ja0, ja1, jb0, jb1;
+  kv_range(qbase, p.T, p.window, ja0, ja1);
+  kv_range(qbase + C::BM, p.T, p.window, jb0, jb1);
+  if (jb1 <= jb0) { jb0 = ja0; jb1 = ja0; }
+  const int j0 = ja0 < jb0 ? ja0 : jb0;
+  const int j1 = ja1 > jb1 ? ja1 : jb1;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    mbar_init(&bars->o_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_free[i], 1);
       mbar_init(&bars->p_full[i], 128);
+      mbar_init(&bars->pv_done[i], 1);
+      mbar_init(&bars->o_full[i], 1);
     }
-    for (int i = 0; i < C::NS; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
       mbar_init(&bars->v_full[i], 1);
-      mbar_init(&bars->kv_empty[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
     }
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -150,124 +194,150 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tbase = bars->tmem_base;
   bool failed = false;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
     if (elect_one()) {
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      mbar_arrive_expect_tx(&bars->q_full, C::Q_BYTES);
-      for (int c = 0; c < C::NCHUNK; ++c)
-        tma_load_4d(sQ + c * C::BM * C::ROWB, &tmq, c * C::CHUNK, q0, h, b, &bars->q_full);
-      for (int i = 0; i < n; ++i) {
-        const int st = i % C::NS;
-        if (i >= C::NS && !wait_or_flag(&bars->kv_empty[st], ((i / C::NS) - 1) & 1, failed)) break;
+      mbar_arrive_expect_tx(&bars->q_full, 2 * C::TILE);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < C::NCHUNK; ++c)
+          tma_load_4d(sQ + t * C::TILE + c * 128 * C::ROWB, &tmq, c * C::CHUNK, qbase + t * C::BM, h, b, &bars->q_full);
+      for (int i = 0; i < j1 - j0 && !failed; ++i) {
         const int kv0 = (j0 + i) * C::BN;
-        uint8_t* k_dst = sK + st * C::KV_BYTES;
-        uint8_t* v_dst = sV + st * C::KV_BYTES;
-        mbar_arrive_expect_tx(&bars->k_full[st], C::KV_BYTES);
+        const int ks = i % C::NK, vs = i % C::NV;
+        if (i >= C::NK && !wait_or_flag(&bars->k_empty[ks], ((i / C::NK) - 1) & 1, failed)) break;
+        mbar_arrive_expect_tx(&bars->k_full[ks], C::TILE);
         for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_4d(k_dst + c * C::BN * C::ROWB, &tmk, c * C::CHUNK, kv0, kvh, b, &bars->k_full[st]);
-        mbar_arrive_expect_tx(&bars->v_full[st], C::KV_BYTES);
+          tma_load_4d(sK + ks * C::TILE + c * 128 * C::ROWB, &tmk, c * C::CHUNK, kv0, kvh, b, &bars->k_full[ks]);
+        if (i >= C::NV && !wait_or_flag(&bars->v_empty[vs], ((i / C::NV) - 1) & 1, failed)) break;
+        mbar_arrive_expect_tx(&bars->v_full[vs], C::TILE);
         for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_4d(v_dst + c * C::BN * C::ROWB, &tmv, c * C::CHUNK, kv0, kvh, b, &bars->v_full[st]);
+          tma_load_4d(sV + vs * C::TILE + c * 128 * C::ROWB, &tmv, c * C::CHUNK, kv0, kvh, b, &bars->v_full[vs]);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       constexpr uint32_t idesc_s = idesc_f16(128, C::BN, BF16 ? 1 : 0, 0, 0);
       constexpr uint32_t idesc_o = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
-      const uint32_t tS = tbase, tO = tbase + 256;
       const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-      if (wait_or_flag(&bars->q_full, 0, failed)) {
-        for (int i = 0; i <= n && !failed; ++i) {
-          if (i < n) {
-            const int st = i % C::NS, bb = i & 1;
-            if (!wait_or_flag(&bars->k_full[st], (i / C::NS) & 1, failed)) break;
-            if (i >= 2 && !wait_or_flag(&bars->s_free[bb], ((i / 2) - 1) & 1, failed)) break;
-            tc_fence_after();
+      const int jlo[2] = {ja0, jb0}, jhi[2] = {ja1, jb1};
+      int s_cnt[2] = {0, 0}, pv_cnt[2] = {0, 0};
+      auto issue_s = [&](int t, int i) {
+        const int ks = i % C::NK;
+        const uint32_t q_s = aQ + t * C::TILE, k_s = aK + ks * C::TILE;
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const int c = (kk * 16) / C::CHUNK;
-              const uint32_t off = ((kk * 16) % C::CHUNK) * 2;
-              const uint64_t da = smem_desc(aQ + c * C::BM * C::ROWB + off, 16, C::SBO, C::SWZ);
-              const uint64_t db = smem_desc(aK + st * C::KV_BYTES + c * C::BN * C::ROWB + off, 16, C::SBO, C::SWZ);
-              mma_ss(tS + bb * 128, da, db, idesc_s, kk > 0);
-            }
-            mma_commit(&bars->s_full[bb]);
-          }
-          if (i >= 1) {
-            const int ip = i - 1, stp = ip % C::NS, bp = ip & 1;
-            if (!wait_or_flag(&bars->p_full[bp], (ip / 2) & 1, failed)) break;
-            if (!wait_or_flag(&bars->v_full[stp], (ip / C::NS) & 1, failed)) break;
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk * 16) / C::CHUNK) * 128 * C::ROWB + ((kk * 16) % C::CHUNK) * 2;
+          mma_ss(tbase + t * 128, smem_desc(q_s + off, 16, C::SBO, C::SWZ), smem_desc(k_s + off, 16, C::SBO, C::SWZ),
+                 idesc_s, kk > 0);
+        }
+        mma_commit(&bars->s_full[t]);
+        ++s_cnt[t];
+      };
+      const int n = j1 - j0;
+      if (wait_or_flag(&bars->q_full, 0, failed) && n > 0) {
+        // prologue: S for the first KV tile
+        if (wait_or_flag(&bars->k_full[0], 0, failed)) {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (j0 >= jlo[t] && j0 < jhi[t]) issue_s(t, 0);
+          mma_commit(&bars->k_empty[0]);
+        }
+        for (int i = 0; i < n && !failed; ++i) {
+          const int j = j0 + i;
+          const int vs = i % C::NV;
+          bool k_next_ready = false;
+          if (!wait_or_flag(&bars->v_full[vs], (i / C::NV) & 1, failed)) break;
+          for (int t = 0; t < 2 && !failed; ++t) {
+            if (j < jlo[t] || j >= jhi[t]) continue;
+            // O_t += P_t V_j once the squareplus warps have written P_t
+            if (!wait_or_flag(&bars->p_full[t], (pv_cnt[t]) & 1, failed)) break;
             tc_fence_after();
+            const uint32_t v_s = aV + vs * C::TILE;
 #pragma unroll
             for (int kk = 0; kk < C::BN / 16; ++kk) {
-              const uint64_t db = smem_desc(aV + stp * C::KV_BYTES + kk * 16 * C::ROWB, C::BN * C::ROWB, C::SBO, C::SWZ);
-              mma_ts(tO, tS + bp * 128 + kk * 8, db, idesc_o, (ip > 0 || kk > 0) ? 1u : 0u);
+              const uint64_t db = smem_desc(v_s + kk * 16 * C::ROWB, 128 * C::ROWB, C::SBO, C::SWZ);
+              mma_ts(tbase + 256 + t * D, tbase + t * 128 + kk * 8, db, idesc_o, (j > jlo[t] || kk > 0) ? 1u : 0u);
             }
-            mma_commit(&bars->kv_empty[stp]);
-            mma_commit(&bars->s_free[bp]);
+            mma_commit(&bars->pv_done[t]);
+            ++pv_cnt[t];
+            if (j + 1 >= jhi[t]) mma_commit(&bars->o_full[t]);
+            // next S_t (reuses the TMEM columns P_t was just read from)
+            if (i + 1 < n && j + 1 >= jlo[t] && j + 1 < jhi[t]) {
+              if (!k_next_ready) {
+                if (!wait_or_flag(&bars->k_full[(i + 1) % C::NK], ((i + 1) / C::NK) & 1, failed)) break;
+                k_next_ready = true;
+              }
+              if (!wait_or_flag(&bars->pv_done[t], (pv_cnt[t] - 1) & 1, failed)) break;
+              tc_fence_after();
+              issue_s(t, i + 1);
+            }
+          }
+          mma_commit(&bars->v_empty[vs]);
+          if (i + 1 < n) {
+            // a tile that only the other Q tile needed next still has to be issued
+            for (int t = 0; t < 2 && !failed; ++t) {
+              const int jn = j + 1;
+              if (jn >= jlo[t] && jn < jhi[t] && !(j >= jlo[t] && j < jhi[t])) {
+                if (!k_next_ready) {
+                  if (!wait_or_flag(&bars->k_full[(i + 1) % C::NK], ((i + 1) / C::NK) & 1, failed)) break;
+                  k_next_ready = true;
+                }
+                tc_fence_after();
+                issue_s(t, i + 1);
+              }
+            }
+            if (k_next_ready) mma_commit(&bars->k_empty[(i + 1) % C::NK]);
           }
         }
-        mma_commit(&bars->o_full);
       }
+      // Q tiles with no work still release their epilogue
+      for (int t = 0; t < 2; ++t)
+        if (jhi[t] <= jlo[t]) mma_commit(&bars->o_full[t]);
     }
   } else {
-    // ------------------------------------------------------------ squareplus warps
+    // ------------------------------------------------------------ squareplus warpgroups
+    const int t = warp >> 2;  // Q tile of this warpgroup
     const int g = warp & 3;
     const int row = 32 * g + lane;
+    const int q0 = qbase + t * C::BM;
     const int q = q0 + row;
+    int jl, jh;
+    kv_range(q0, p.T, p.window, jl, jh);
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
+    const uint32_t tS = tl + t * 128;
     float rsum = 4e-12f;  // 4 * EPS (y is carried as 4y)
-    for (int i = 0; i < n; ++i) {
-      const int bb = i & 1;
-      const int k0 = (j0 + i) * C::BN;
-      if (!warp_wait_or_flag(&bars->s_full[bb], (i / 2) & 1, failed)) break;
+    for (int j = jl, it = 0; j < jh; ++j, ++it) {
+      if (!warp_wait_or_flag(&bars->s_full[t], it & 1, failed)) break;
       tc_fence_after();
+      const int k0 = j * C::BN;
       const bool need_mask = (k0 + C::BN - 1 > q0) || (k0 + C::BN > p.T) ||
                              (p.window > 0 && q0 + C::BM - 1 - k0 >= p.window);
-#pragma unroll
-      for (int c = 0; c < C::BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tl + bb * 128 + c * 32, r);
-        tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float yv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float a = fmaf(__uint_as_float(r[e + u]), p.scale2, -1.0f);
-            const float w = fmaf(a, a, 4.0f);
-            const float t = EXACT ? a + sqrtf(w) : fmaf(w, rsqrtf(w), a);
-            float y = t * t;
-            if (need_mask) {
-              const int k = k0 + c * 32 + e + u;
-              const bool ok = (k <= q) && (k < p.T) && (p.window <= 0 || q - k < p.window);
-              y = ok ? y : 0.f;
-            }
-            yv[u] = y;
-          }
-          rsum += yv[0] + yv[1];
-          pk[e / 2] = BF16 ? pack2_bf16(yv[0], yv[1]) : pack2_f16(yv[0], yv[1]);
-        }
-        tmem_st16(tl + bb * 128 + c * 16, pk);
+      if (need_mask) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c)
+          rsum += squareplus_chunk<BF16, EXACT, true>(tS + c * 32, tS + c * 16, p.scale2, k0 + c * 32, q, p.T, p.window);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c)
+          rsum += squareplus_chunk<BF16, EXACT, false>(tS + c * 32, tS + c * 16, p.scale2, 0, 0, 0, 0);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->p_full[bb]);
+      mbar_arrive(&bars->p_full[t]);
     }
-    if (warp_wait_or_flag(&bars->o_full, 0, failed)) {
+    if (warp_wait_or_flag(&bars->o_full[t], 0, failed) && jh > jl) {
       tc_fence_after();
       const float inv = 1.0f / rsum;
       const bool live = q < p.T;
       uint8_t* orow = static_cast<uint8_t*>(p.o) + 2 * ((int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)q * p.so_s);
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tl + 256 + c * 32, r);  // all lanes: .sync.aligned
+        tmem_ld32(tl + 256 + t * D + c * 32, r);  // all lanes: .sync.aligned
         tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
@@ -287,7 +357,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tbase, C::TMEM_COLS);
   }
@@ -348,12 +418,12 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, floa
   p.Hq = (int)Hq;
   p.Hkv = (int)Hkv;
   p.T = (int)T;
-  p.nqt = (int)((T + C::BM - 1) / C::BM);
+  p.npairs = (int)((T + 2 * C::BM - 1) / (2 * C::BM));
   p.window = (int)window;
   p.scale2 = 2.0f * scale;
   auto kern = flash_fwd_kernel<D, BF16, EXACT>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  dim3 grid(p.nqt, (unsigned)(B * Hq));
+  dim3 grid(p.npairs, (unsigned)(B * Hq));
   kern<<<grid, C::THREADS, C::SMEM, st>>>(mq, mk, mv, p);
   return SA_OK;
 }
