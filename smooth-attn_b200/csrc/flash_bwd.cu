@@ -395,6 +395,358 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// D = 128 backward: 64-row query tiles, double-buffered S^T / dP^T in TMEM.
+//
+// TMEM (512 columns): S^T_b @ 64b, dP^T_b (later dQ^T_b) @ 128 + 64b,
+// dK @ 256, dV @ 384.  dQ is produced transposed, dQ^T = K^T dS^T (M = the
+// 128 head-dim rows, N = 64 query columns), into the dP^T columns the
+// elementwise stage has just consumed, so every accumulator fits and the
+// S/dP MMAs of tile i+1 run while tile i's elementwise stage runs.
+// Warps: 0-7 elementwise (two warpgroups, 32 query columns each), 8-11 dQ
+// drain (TMEM lane = head-dim index: coalesced fp32 atomics), 12 TMA, 13 MMA.
+// ---------------------------------------------------------------------------
+struct Bwd128 {
+  static constexpr int D = 128, BN = 128, BQ = 64, NS = 3;
+  static constexpr int KV_TILE = 128 * D * 2;  // 2 chunks of 128 rows x 128 B
+  static constexpr int Q_TILE = BQ * D * 2;    // 2 chunks of 64 rows x 128 B
+  static constexpr int DS_TILE = BN * BQ * 2;  // [128 kv][64 q], 128 B swizzle
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + KV_TILE;
+  static constexpr int OFF_Q = OFF_V + KV_TILE;
+  static constexpr int OFF_DO = OFF_Q + NS * Q_TILE;
+  static constexpr int OFF_DS = OFF_DO + NS * Q_TILE;
+  static constexpr int OFF_VEC = OFF_DS + 2 * DS_TILE;  // invR[2][64], delta[2][64]
+  static constexpr int OFF_BAR = OFF_VEC + 4 * 64 * 4;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int THREADS = 448;
+};
+
+struct Bwd128Bars {
+  uint64_t kv_full;
+  uint64_t q_full[3], q_empty[3];
+  uint64_t s_full[2], p_ready[2], mm2_done[2], dq_free[2];
+  uint64_t all_done;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void ew_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+
+// AND of `v` over the 256 elementwise threads (also a barrier among them).
+__device__ __forceinline__ bool ew_all(bool v) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 2, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)v)
+      : "memory");
+  return out != 0;
+}
+
+template <bool BF16, bool EXACT, bool MASK>
+__device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, uint8_t* dsrow, int r,
+                                             const float* vInvR, const float* vDelta, float scale2, float c4s, int n,
+                                             int q0, int T, int window) {
+  uint32_t sv[32], dv[32];
+  tmem_ld32(tS + 32 * w2, sv);
+  tmem_ld32(tP + 32 * w2, dv);
+  tmem_ld_wait();
+  uint32_t pk[16], dk[16];
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) {
+    const float4 ir = *reinterpret_cast<const float4*>(vInvR + 32 * w2 + e);
+    const float4 de = *reinterpret_cast<const float4*>(vDelta + 32 * w2 + e);
+    const float irs[4] = {ir.x, ir.y, ir.z, ir.w};
+    const float des[4] = {de.x, de.y, de.z, de.w};
+    float pv[4], dsv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
+      const float w = fmaf(a, a, 4.0f);
+      const float rs = rsqrtf(w);
+      const float sq = EXACT ? sqrtf(w) : w * rs;
+      const float sp = 0.5f * (a + sq);
+      const float spp = 0.5f * fmaf(a, rs, 1.0f);
+      float pp = sp * sp * irs[u];
+      float ds = (__uint_as_float(dv[e + u]) - des[u]) * irs[u] * (c4s * sp * spp);
+      if (MASK) {
+        const int q = q0 + 32 * w2 + e + u;
+        const bool ok = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
+        pp = ok ? pp : 0.f;
+        ds = ok ? ds : 0.f;
+      }
+      pv[u] = pp;
+      dsv[u] = ds;
+    }
+    pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
+    pk[e / 2 + 1] = BF16 ? pack2_bf16(pv[2], pv[3]) : pack2_f16(pv[2], pv[3]);
+    dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
+    dk[e / 2 + 1] = BF16 ? pack2_bf16(dsv[2], dsv[3]) : pack2_f16(dsv[2], dsv[3]);
+  }
+  // both warpgroups must have read their S^T columns before P overwrites them
+  ew_sync();
+  tmem_st16(tS + 16 * w2, pk);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int piece = (w2 * 4 + j) ^ (r & 7);
+    *reinterpret_cast<uint4*>(dsrow + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+  }
+}
+
+template <bool BF16, bool EXACT>
+__global__ void __launch_bounds__(448, 1)
+    flash_bwd128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
+                        BwdParams p) {
+  using C = Bwd128;
+  constexpr int D = C::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sDO = smem + C::OFF_DO;
+  uint8_t* sDS = smem + C::OFF_DS;
+  float* vInvR = reinterpret_cast<float*>(smem + C::OFF_VEC);  // [2][64]
+  float* vDelta = vInvR + 128;                                  // [2][64]
+  Bwd128Bars* bars = reinterpret_cast<Bwd128Bars*>(smem + C::OFF_BAR);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * C::BN;
+  const int b = blockIdx.y / p.Hkv, kvh = blockIdx.y % p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  const int nqt = (p.T + C::BQ - 1) / C::BQ;
+  const int qt_first = n0 / C::BQ;
+  int qt_last = nqt - 1;
+  if (p.window > 0) {
+    const int l = (n0 + C::BN - 1 + p.window - 1) / C::BQ;
+    if (l < qt_last) qt_last = l;
+  }
+  const int per_head = qt_last - qt_first + 1;
+  const int ntiles = G * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars->q_full[i], 1);
+      mbar_init(&bars->q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_ready[i], 256);
+      mbar_init(&bars->mm2_done[i], 1);
+      mbar_init(&bars->dq_free[i], 128);
+    }
+    mbar_init(&bars->all_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 13) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  bool failed = false;
+
+  if (warp == 12) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      tma_prefetch_desc(&tmdo);
+      mbar_arrive_expect_tx(&bars->kv_full, 2 * C::KV_TILE);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_4d(sK + c * 128 * 128, &tmk, c * 64, n0, kvh, b, &bars->kv_full);
+        tma_load_4d(sV + c * 128 * 128, &tmv, c * 64, n0, kvh, b, &bars->kv_full);
+      }
+      for (int it = 0; it < ntiles && !failed; ++it) {
+        const int st = it % C::NS;
+        if (it >= C::NS && !b_wait(&bars->q_empty[st], ((it / C::NS) - 1) & 1, failed)) break;
+        const int h = kvh * G + it / per_head;
+        const int q0 = (qt_first + it % per_head) * C::BQ;
+        mbar_arrive_expect_tx(&bars->q_full[st], 2 * C::Q_TILE);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_4d(sQ + st * C::Q_TILE + c * C::BQ * 128, &tmq, c * 64, q0, h, b, &bars->q_full[st]);
+          tma_load_4d(sDO + st * C::Q_TILE + c * C::BQ * 128, &tmdo, c * 64, q0, h, b, &bars->q_full[st]);
+        }
+      }
+    }
+  } else if (warp == 13) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr int ab = BF16 ? 1 : 0;
+      constexpr uint32_t id_s = idesc_f16(128, C::BQ, ab, 0, 0);  // S^T, dP^T
+      constexpr uint32_t id_kv = idesc_f16(128, D, ab, 0, 1);     // dV, dK: B (dO / Q) MN-major
+      constexpr uint32_t id_dq = idesc_f16(128, C::BQ, ab, 1, 1); // dQ^T: A = K^T MN-major, B = dS^T MN-major
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
+      const uint32_t aDS = smem_u32(sDS);
+      const uint32_t tDK = tbase + 256, tDV = tbase + 384;
+      auto issue_sdp = [&](int it) {
+        const int st = it % C::NS, bb = it & 1;
+        const uint32_t q_s = aQ + st * C::Q_TILE, do_s = aDO + st * C::Q_TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;  // K/V: 128-row chunks
+          const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;  // Q/dO: 64-row chunks
+          mma_ss(tbase + bb * 64, smem_desc(aK + koff, 16, 1024, SW_128B), smem_desc(q_s + qoff, 16, 1024, SW_128B),
+                 id_s, kk > 0);
+          mma_ss(tbase + 128 + bb * 64, smem_desc(aV + koff, 16, 1024, SW_128B),
+                 smem_desc(do_s + qoff, 16, 1024, SW_128B), id_s, kk > 0);
+        }
+        mma_commit(&bars->s_full[bb]);
+      };
+      if (b_wait(&bars->kv_full, 0, failed) && ntiles > 0 && b_wait(&bars->q_full[0], 0, failed)) {
+        tc_fence_after();
+        issue_sdp(0);
+        for (int it = 0; it < ntiles && !failed; ++it) {
+          const int bb = it & 1, st = it % C::NS;
+          if (it + 1 < ntiles) {
+            const int nx = it + 1;
+            if (!b_wait(&bars->q_full[nx % C::NS], (nx / C::NS) & 1, failed)) break;
+            if (it >= 1) {
+              if (!b_wait(&bars->mm2_done[bb ^ 1], ((it - 1) >> 1) & 1, failed)) break;
+              if (!b_wait(&bars->dq_free[bb ^ 1], ((it - 1) >> 1) & 1, failed)) break;
+            }
+            tc_fence_after();
+            issue_sdp(nx);
+          }
+          if (!b_wait(&bars->p_ready[bb], (it >> 1) & 1, failed)) break;
+          tc_fence_after();
+          const uint32_t q_s = aQ + st * C::Q_TILE, do_s = aDO + st * C::Q_TILE;
+          const uint32_t ds_s = aDS + bb * C::DS_TILE;
+#pragma unroll
+          for (int kk = 0; kk < C::BQ / 16; ++kk) {  // K = 64 query rows
+            const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+            const uint64_t b_do = smem_desc(do_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
+            const uint64_t b_q = smem_desc(q_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
+            mma_ts(tDV, tbase + bb * 64 + kk * 8, b_do, id_kv, acc);
+            mma_ss(tDK, smem_desc(ds_s + kk * 32, 16, 1024, SW_128B), b_q, id_kv, acc);
+          }
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk) {  // K = 128 KV rows
+            const uint64_t a_kt = smem_desc(aK + kk * 16 * 128, 128 * 128, 1024, SW_128B);
+            const uint64_t b_ds = smem_desc(ds_s + kk * 16 * 128, C::DS_TILE, 1024, SW_128B);
+            mma_ss(tbase + 128 + bb * 64, a_kt, b_ds, id_dq, kk > 0);
+          }
+          mma_commit(&bars->mm2_done[bb]);
+          mma_commit(&bars->q_empty[st]);
+        }
+      }
+      mma_commit(&bars->all_done);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ dQ drain
+    const int g = warp & 3;
+    const int d = 32 * g + lane;  // TMEM lane = head-dim index of dQ^T
+    const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
+    for (int it = 0; it < ntiles && !failed; ++it) {
+      const int bb = it & 1;
+      if (!b_warp_wait(&bars->mm2_done[bb], (it >> 1) & 1, failed)) break;
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tl + 128 + bb * 64, v0);
+      tmem_ld32(tl + 128 + bb * 64 + 32, v1);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->dq_free[bb]);
+      const int h = kvh * G + it / per_head;
+      const int q0 = (qt_first + it % per_head) * C::BQ;
+      float* dst = p.dq_acc + (((int64_t)b * p.Hq + h) * p.T + q0) * D + d;
+      const int lim = p.T - q0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < lim) atomicAdd(dst + (int64_t)j * D, __uint_as_float(v0[j]));
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (32 + j < lim) atomicAdd(dst + (int64_t)(32 + j) * D, __uint_as_float(v1[j]));
+    }
+  } else {
+    // ------------------------------------------------------------ elementwise warpgroups
+    const int w2 = warp >> 2;  // query-column half
+    const int g = warp & 3;
+    const int r = 32 * g + lane;  // TMEM lane = KV row
+    const int n = n0 + r;
+    const int tid = threadIdx.x;  // 0..255
+    const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
+    const float scale2 = 2.0f * p.scale, c4s = 4.0f * p.scale;
+    float pre = 0.f;
+    auto prefetch = [&](int it) {  // threads 0..63: invR, 64..127: delta
+      if (tid >= 128) return;
+      const int h = kvh * G + it / per_head;
+      const int qq = (qt_first + it % per_head) * C::BQ + (tid & 63);
+      const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + qq;
+      const bool ok = it < ntiles && qq < p.T;
+      pre = !ok ? 0.f : (tid < 64 ? 1.0f / __ldg(p.rowsum + idx) : __ldg(p.delta + idx));
+    };
+    prefetch(0);
+    for (int it = 0; it < ntiles && !failed; ++it) {
+      const int bb = it & 1;
+      const int q0 = (qt_first + it % per_head) * C::BQ;
+      ew_sync();
+      if (tid < 128) (tid < 64 ? vInvR : vDelta)[bb * 64 + (tid & 63)] = pre;
+      ew_sync();
+      prefetch(it + 1);
+      // all 256 threads leave together on a timeout (the chunk below has a named barrier)
+      if (!ew_all(mbar_wait(&bars->s_full[bb], (it >> 1) & 1))) {
+        if (tid == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const bool need_mask = (q0 < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.T) ||
+                             (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
+      uint8_t* dsrow = sDS + bb * C::DS_TILE + r * 128;
+      if (need_mask)
+        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
+                                        vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
+      else
+        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
+                                         vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->p_ready[bb]);
+    }
+    // epilogue: warpgroup 0 writes dK, warpgroup 1 writes dV (TMEM lane = KV row)
+    if (b_warp_wait(&bars->all_done, 0, failed)) {
+      tc_fence_after();
+      const bool live = n < p.T;
+      uint8_t* base = static_cast<uint8_t*>(w2 ? p.dv : p.dk) +
+                      2 * (w2 ? ((int64_t)b * p.sdv_b + (int64_t)kvh * p.sdv_h + (int64_t)n * p.sdv_s)
+                              : ((int64_t)b * p.sdk_b + (int64_t)kvh * p.sdk_h + (int64_t)n * p.sdk_s));
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tl + 256 + w2 * 128 + c * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          pk[e / 2] = BF16 ? pack2_bf16(__uint_as_float(v[e]), __uint_as_float(v[e + 1]))
+                           : pack2_f16(__uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+        if (live) {
+          uint4* dst = reinterpret_cast<uint4*>(base + c * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 13) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 // delta = rowsum(dO * O) (fp32) and dq_acc = 0.  One warp per query row.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) flash_bwd_prep(const T* __restrict__ o, const T* __restrict__ dout,
@@ -479,10 +831,20 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
   p.T = (int)T;
   p.window = (int)window;
   p.scale = scale;
-  auto kern = flash_bwd_kernel<D, BF16, EXACT>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   dim3 grid((unsigned)((T + C::BN - 1) / C::BN), (unsigned)(B * Hkv));
-  kern<<<grid, 192, C::SMEM, st>>>(mq, mk, mv, mdo, p);
+  if constexpr (D == 128) {
+    CUtensorMap mq64, mdo64;
+    if (!make_map_4d(&mq64, q, BF16, B, Hq, T, D, qs, 64, Bwd128::BQ) ||
+        !make_map_4d(&mdo64, dout, BF16, B, Hq, T, D, dos, 64, Bwd128::BQ))
+      return SA_ERR_ALIGN;
+    auto kern = flash_bwd128_kernel<BF16, EXACT>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Bwd128::SMEM);
+    kern<<<grid, Bwd128::THREADS, Bwd128::SMEM, st>>>(mq64, mk, mv, mdo64, p);
+  } else {
+    auto kern = flash_bwd_kernel<D, BF16, EXACT>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    kern<<<grid, 192, C::SMEM, st>>>(mq, mk, mv, mdo, p);
+  }
   const int64_t nthreads = rows * (D / 8);
   flash_bwd_dq_convert<T16, D><<<(unsigned)((nthreads + 255) / 256), 256, 0, st>>>(
       dq_acc, static_cast<T16*>(dq), rows, (int)Hq, (int)T, dqs[0], dqs[1], dqs[2]);
