@@ -145,6 +145,30 @@ SA_API int sa_flash_bwd(const void* q, const void* k, const void* v, const void*
                  const int64_t* dv_strides, float scale, int64_t window_size, int exact_math, int dtype,
                  void* stream);
 
+/*
+ * Allocation-free sa_flash_bwd, for callers that cannot allocate device
+ * memory (inside a stream capture that must not allocate, host frameworks
+ * that own all device memory, latency-critical loops).  No counterpart in
+ * the reference: the reference always allocates its scratch with torch.
+ * Same arguments and results as sa_flash_bwd, minus the workspace: the
+ * scratch is a fixed file-scope device array of
+ * sa_flash_bwd_noalloc_max_bytes() bytes (32 MiB) that every GPU loading the
+ * library holds until exit.  Problems whose sa_flash_bwd_workspace_size()
+ * exceeds it are rejected with SA_ERR_ARG before anything is launched.
+ * The first call on a device looks up the array's device address (make that
+ * first call before any stream capture).  All calls share the one array:
+ * calls that overlap on the GPU (other streams, other threads) race and give
+ * wrong results; serialise them.  Calls no cudaMalloc / cudaFree.
+ */
+SA_API int64_t sa_flash_bwd_noalloc_max_bytes(void);
+SA_API int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                const float* rowsum, void* dq, void* dk, void* dv, int64_t B, int64_t Hq,
+                                int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides,
+                                const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                                const int64_t* dv_strides, float scale, int64_t window_size, int exact_math,
+                                int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -930,3 +930,63 @@ extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const v
   if (rc != SA_OK) return rc;
   return sa_record_cuda_error(cudaGetLastError());
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of sa_flash_bwd.
+//
+// Some callers cannot call cudaMalloc: code running inside a CUDA-graph
+// capture that must not allocate, plugins whose host framework owns all
+// device memory and forbids allocation, or real-time loops where an
+// allocator call could stall.  For them the backward's scratch (the fp32 dQ
+// accumulator and the per-row delta) lives in a fixed, file-scope device
+// array instead of a caller-provided workspace.  Every GPU that loads this
+// library holds the array (SA_NOALLOC_SCRATCH_BYTES) until the process exits.
+// ---------------------------------------------------------------------------
+
+#define SA_NOALLOC_SCRATCH_BYTES (32ll << 20)  // 32 MiB
+
+static __device__ __align__(256) unsigned char g_bwd_noalloc_scratch[SA_NOALLOC_SCRATCH_BYTES];
+
+#include <mutex>
+
+// Device address of the scratch array for the current device.  In host code
+// the array's name is only a host-side handle; the real device address is
+// looked up once per device (with that device current) and cached.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return sa_record_cuda_error(e);
+  if (dev < 0 || dev >= 64) return SA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return sa_record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return SA_OK;
+}
+
+extern "C" int64_t sa_flash_bwd_noalloc_max_bytes(void) { return SA_NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                    const float* rowsum, void* dq, void* dk, void* dv, int64_t B, int64_t Hq,
+                                    int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides,
+                                    const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
+                                    const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
+                                    const int64_t* dv_strides, float scale, int64_t window_size, int exact_math,
+                                    int dtype, void* stream) {
+  const int64_t need = sa_flash_bwd_workspace_size(B, Hq, Hkv, T, D);
+  if (need > SA_NOALLOC_SCRATCH_BYTES) return SA_ERR_ARG;  // problem too large for the fixed scratch
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != SA_OK) return rc;
+  }
+  return sa_flash_bwd(q, k, v, o, dout, rowsum, dq, dk, dv, scratch, SA_NOALLOC_SCRATCH_BYTES, B, Hq, Hkv, T, D,
+                      q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides,
+                      scale, window_size, exact_math, dtype, stream);
+}

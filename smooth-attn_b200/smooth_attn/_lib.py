@@ -41,6 +41,11 @@ SIGNATURES = {
     "sa_flash_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
                             _i64p, _i64p, _i64p, _i64p, _f, _i64, _int, _int, _p]),
     "sa_flash_bwd_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "sa_flash_bwd_noalloc_max_bytes": (_i64, []),
+    "sa_flash_bwd_noalloc": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                    _i64, _i64, _i64, _i64, _i64,
+                                    _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
+                                    _f, _i64, _int, _int, _p]),
     "sa_flash_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
                             _i64, _i64, _i64, _i64, _i64,
                             _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
