@@ -169,7 +169,12 @@ def run_ours(args):
 
     world, rank, local = dist_setup(args.gpus)
     hbm, tf_burst, tf_sus, peak_kind = peaks()
-    B, H, L = NORM_CFG["B"], NORM_CFG["H"], NORM_CFG["L"]
+    if args.only == "flash":
+        flash = run_flash(args, world, rank, tf_burst, tf_sus, peak_kind)
+        if rank == 0:
+            print(json.dumps({"metric": "fused squareplus-attn fwd+bwd TFLOP/s", "n_gpus": world, **flash}), flush=True)
+        return
+    B, H, L = args.norm_batch, NORM_CFG["H"], NORM_CFG["L"]
     m_loc = B * H  # this rank's block of the global [N*B, H, L, L] batch
     M = m_loc * world
     gen = torch.Generator().manual_seed(1234 + rank)
@@ -207,7 +212,7 @@ def run_ours(args):
     e2e_val = bytes_all / (e2e_ms * 1e-3) / 1e9
 
     flash = None
-    if not args.skip_flash:
+    if args.only == "all" and not args.skip_flash:
         flash = run_flash(args, world, rank, tf_burst, tf_sus, peak_kind)
 
     cpu = None
@@ -250,7 +255,7 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
     import smooth_attn as sa
     from oracle import sa_oracle as O
 
-    B, H, T, D = FLASH_CFG["B"], FLASH_CFG["H"], FLASH_CFG["T"], FLASH_CFG["D"]
+    B, H, T, D = (int(v) for v in args.flash_shape.split(","))
     b_loc = B * H  # this rank's block of (b,h) heads, laid out as [1, B*H, T, D]
     gen = torch.Generator().manual_seed(4321 + rank)
     mk = lambda: torch.randn(1, b_loc, T, D, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)  # noqa: E731
@@ -263,7 +268,7 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
 
     def step():
         o = sa.sp2norm_flash_attention(q, k, v)
-        torch.autograd.backward(o, do)
+        torch.autograd.grad(o, (q, k, v), do)  # fresh dq/dk/dv, no .grad accumulation kernels
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -277,7 +282,9 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
     return {
         "metric": "fused squareplus-attn fwd+bwd TFLOP/s", "value": round(flops_all / (ms * 1e-3) / 1e12, 1),
         "unit": "TFLOP/s", "ms_per_step": round(ms, 3),
-        "config": {"workload": "BASELINE configs[3]", "shape": [B, H, T, D], "dtype": "bf16", "causal": True},
+        "config": {"workload": "BASELINE configs[3]" if [B, H, T, D] == [4, 32, 4096, 128] else "custom",
+                   "shape": [B, H, T, D], "dtype": "bf16", "causal": True,
+                   "parallelism": f"dp{world}: one [{B},{H},{T},{D}] block of heads per GPU, no collective"},
         "roofline": {"bound": "tensor", "achieved": round(flops_loc / (ms * 1e-3) / 1e12, 1), "peak": tf_sus,
                      "unit": "TFLOP/s", "frac": round(flops_loc / (ms * 1e-3) / 1e12 / tf_sus, 4),
                      "peak_kind": f"{peak_kind} bf16_tflops_sustained"},
@@ -349,6 +356,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--skip-flash", action="store_true")
+    ap.add_argument("--only", choices=("all", "norm", "flash"), default="all",
+                    help="run one workload only (small-case profiling)")
+    ap.add_argument("--norm-batch", type=int, default=NORM_CFG["B"],
+                    help="B of the causal-norm workload [B,16,2048,2048] (BASELINE: 8)")
+    ap.add_argument("--flash-shape", default=",".join(str(FLASH_CFG[k]) for k in "BHTD"),
+                    help="B,H,T,D of the attention workload (BASELINE: 4,32,4096,128)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--traffic-bytes", type=float, default=None,

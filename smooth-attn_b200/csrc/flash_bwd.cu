@@ -89,7 +89,7 @@ __device__ __forceinline__ void bwd_chunk(uint32_t tl, int c, uint8_t* sDS, int 
       const int m = c * 32 + e + u;
       const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
       const float w = fmaf(a, a, 4.0f);
-      const float rs = rsqrtf(w);
+      const float rs = rsqrt_approx(w);
       const float sq = EXACT ? sqrtf(w) : w * rs;
       const float sp = 0.5f * (a + sq);
       const float spp = 0.5f * fmaf(a, rs, 1.0f);
@@ -466,7 +466,7 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
     for (int u = 0; u < 4; ++u) {
       const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
       const float w = fmaf(a, a, 4.0f);
-      const float rs = rsqrtf(w);
+      const float rs = rsqrt_approx(w);
       const float sq = EXACT ? sqrtf(w) : w * rs;
       const float sp = 0.5f * (a + sq);
       const float spp = 0.5f * fmaf(a, rs, 1.0f);

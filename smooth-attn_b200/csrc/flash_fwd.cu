@@ -126,7 +126,7 @@ __device__ __forceinline__ float squareplus_chunk(uint32_t taddr_s, uint32_t tad
     for (int u = 0; u < 2; ++u) {
       const float a = fmaf(__uint_as_float(r[e + u]), scale2, -1.0f);
       const float w = fmaf(a, a, 4.0f);
-      const float t = EXACT ? a + sqrtf(w) : fmaf(w, rsqrtf(w), a);
+      const float t = EXACT ? a + sqrtf(w) : fmaf(w, rsqrt_approx(w), a);
       float y = t * t;  // 4 * squareplus(a)^2
       if (MASK) {
         const int k = kbase + e + u;

@@ -231,13 +231,32 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t phase) {
   return ok;
 }
 
-// fwd: CH = 16-byte vectors per lane held in registers (KEEP_Y), or 0 for rows
-// too long to hold (then y is recomputed from shared memory in a second pass).
-template <typename T, int CH, bool CAUSAL>
+// 2^p * squareplus(a)^p with a = c1*x + c0 (c1 = alpha, c0 = -alpha*theta).
+// t = a + sqrt(a^2+4) is exactly 2*squareplus(a); carrying y' = t^p = 2^p y
+// instead of y drops the two 0.5 factors and scales every y, the row sum and
+// EPS by the same power of two, so out = y'/S' equals y/S to the rounding.
+// (For the default family, fma(x, 2, -1) is bit-identical to the
+// reference's x + x - 1.)
+template <bool P2>
+__device__ __forceinline__ float y_scaled(float x, float c1, float c0, int power) {
+  const float a = fmaf(x, c1, c0);
+  const float u = fmaf(a, a, 4.0f);
+  const float t = fmaf(u, rsqrt_approx(u), a);
+  if (P2) return t * t;
+  float y = t;
+  if (power >= 2) y *= t;
+  if (power == 3) y *= t;
+  return y;
+}
+
+// fwd: CH = 16-byte vectors per lane held in registers, or 0 for rows too
+// long to hold (then y is recomputed from shared memory in a second pass).
+template <typename T, int CH, bool CAUSAL, bool P2>
 __global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __restrict__ x, T* __restrict__ out,
                                                                  float* __restrict__ rowsum, int64_t rows, int cols,
-                                                                 int64_t ldx, int64_t ldo, float alpha, float theta,
-                                                                 int power, int nst, int sb) {
+                                                                 int64_t ldx, int64_t ldo, float c1, float c0,
+                                                                 int power, float eps_s, float s_unscale, int nst,
+                                                                 int sb) {
   constexpr int VEC = 16 / sizeof(T);
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -269,6 +288,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __rest
     if (!warp_wait(&bars[s], (uint32_t)(k / nst) & 1u)) return;
     const int q = CAUSAL ? (int)(row % cols) : cols - 1;
     const int nvis = (q + VEC) / VEC;
+    const int qe = q - (nvis - 1) * VEC;  // last visible element inside the diagonal vector
     const uint8_t* slot = ring + (size_t)s * sb;
     T* orow = out + row * ldo;
     float sum = 0.f;
@@ -277,57 +297,67 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __rest
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
         const int v = lane + 32 * c;
+        if (32 * c < nvis) {  // warp-uniform
+          if (v < nvis) {
+            float xf[VEC];
+            unpack<T, VEC>(slot + (size_t)v * 16, xf);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) y[c][e] = 0.f;
-        if (32 * c < nvis && v < nvis) {
-          Pack<T, VEC> p;
-          p.u = *reinterpret_cast<const uint4*>(slot + (size_t)v * 16);
+            for (int e = 0; e < VEC; ++e) y[c][e] = y_scaled<P2>(xf[e], c1, c0, power);
+            if (CAUSAL && v == nvis - 1) {
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) {
-            float yy = family_y(p.get(e), alpha, theta, power);
-            if (CAUSAL && v * VEC + e > q) yy = 0.f;
-            y[c][e] = yy;
-            sum += yy;
+              for (int e = 0; e < VEC; ++e) y[c][e] = e > qe ? 0.f : y[c][e];
+            }
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) sum += y[c][e];
           }
         }
       }
       __syncwarp();
       if (lane == 0 && row + nst * nw < rows) issue(row + nst * nw, s);  // slot consumed
-      const float S = warp_sum(sum) + SA_EPS;
+      const float S = warp_sum(sum) + eps_s;
       const float inv = 1.0f / S;
-      if (rowsum != nullptr && lane == 0) rowsum[row] = S;
+      if (rowsum != nullptr && lane == 0) rowsum[row] = S * s_unscale;
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
         const int v = lane + 32 * c;
         if (v < nvec) {
           Pack<T, VEC> o;
+          if (32 * c < nvis && v < nvis) {
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) o.set(e, y[c][e] * inv);
+            for (int e = 0; e < VEC; ++e) o.set(e, y[c][e] * inv);
+          } else {
+            o.zero();
+          }
           store_stream(orow + (int64_t)v * VEC, o);
         }
       }
     } else {
-      for (int v = lane; v < nvis; v += 32) {
-        Pack<T, VEC> p;
-        p.u = *reinterpret_cast<const uint4*>(slot + (size_t)v * 16);
+      const int nfull = CAUSAL ? nvis - 1 : nvis;  // vectors with no masked element
+      for (int v = lane; v < nfull; v += 32) {
+        float xf[VEC];
+        unpack<T, VEC>(slot + (size_t)v * 16, xf);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const float yy = family_y(p.get(e), alpha, theta, power);
-          sum += (CAUSAL && v * VEC + e > q) ? 0.f : yy;
-        }
+        for (int e = 0; e < VEC; ++e) sum += y_scaled<P2>(xf[e], c1, c0, power);
       }
-      const float S = warp_sum(sum) + SA_EPS;
+      if (CAUSAL && lane == (nvis - 1) % 32) {
+        float xf[VEC];
+        unpack<T, VEC>(slot + (size_t)(nvis - 1) * 16, xf);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (e <= qe) sum += y_scaled<P2>(xf[e], c1, c0, power);
+      }
+      const float S = warp_sum(sum) + eps_s;
       const float inv = 1.0f / S;
-      if (rowsum != nullptr && lane == 0) rowsum[row] = S;
+      if (rowsum != nullptr && lane == 0) rowsum[row] = S * s_unscale;
       for (int v = lane; v < nvec; v += 32) {
         Pack<T, VEC> o;
         if (v < nvis) {
-          Pack<T, VEC> p;
-          p.u = *reinterpret_cast<const uint4*>(slot + (size_t)v * 16);
+          float xf[VEC];
+          unpack<T, VEC>(slot + (size_t)v * 16, xf);
 #pragma unroll
           for (int e = 0; e < VEC; ++e) {
-            const float yy = family_y(p.get(e), alpha, theta, power);
-            o.set(e, (CAUSAL && v * VEC + e > q) ? 0.f : yy * inv);
+            const float yy = y_scaled<P2>(xf[e], c1, c0, power);
+            o.set(e, (CAUSAL && v == nvis - 1 && e > qe) ? 0.f : yy * inv);
           }
         } else {
           o.zero();
@@ -342,12 +372,15 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __rest
 
 // bwd: a slot holds the visible part of the x row followed (at offset gofs)
 // by the visible part of the g row; y is recomputed in the second pass.
-template <typename T, typename TG, bool CAUSAL>
+//   t = 2 sp, w = 2 sp' = 1 + a rsqrt(a^2+4)
+//   dy/dx = alpha p sp^(p-1) sp' = kp t^(p-1) w,   kp = alpha p / 2^p
+template <typename T, typename TG, bool CAUSAL, bool P2>
 __global__ void __launch_bounds__(kBulkWarps * 32) norm_bwd_bulk(const T* __restrict__ x, const TG* __restrict__ g,
                                                                  const float* __restrict__ rowsum, T* __restrict__ dx,
                                                                  int64_t rows, int cols, int64_t ldx, int64_t ldg,
-                                                                 int64_t ldd, float alpha, float theta, int power,
-                                                                 int nst, int sb, int gofs) {
+                                                                 int64_t ldd, float c1, float c0, int power,
+                                                                 float eps_s, float s_scale, float kp, int nst, int sb,
+                                                                 int gofs) {
   constexpr int VEC = 16 / sizeof(T);
   constexpr int GB = VEC * (int)sizeof(TG);  // bytes of g per x vector (8, 16 or 32)
   extern __shared__ __align__(128) uint8_t smem[];
@@ -362,7 +395,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_bwd_bulk(const T* __rest
     const int q = CAUSAL ? (int)(row % cols) : cols - 1;
     const int nv = (q + VEC) / VEC;
     const uint32_t bx = (uint32_t)nv * 16u;
-    const uint32_t bg = ((uint32_t)nv * GB + 15u) & ~15u;  // g rows are 16 B aligned; may over-read <16 B
+    const uint32_t bg = ((uint32_t)nv * GB + 15u) & ~15u;  // in-row: cols*sizeof(TG) % 16 == 0
     mbar_arrive_expect_tx(&bars[s], bx + bg);
     bulk_g2s(ring + (size_t)s * sb, x + row * ldx, bx, &bars[s]);
     bulk_g2s(ring + (size_t)s * sb + gofs, g + row * ldg, bg, &bars[s]);
@@ -377,52 +410,55 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_bwd_bulk(const T* __rest
   }
   __syncwarp();
 
-  const float ap = alpha * (float)power;
   int k = 0;
   for (int64_t row = first; row < rows; row += nw, ++k) {
     const int s = k % nst;
     if (!warp_wait(&bars[s], (uint32_t)(k / nst) & 1u)) return;
     const int q = CAUSAL ? (int)(row % cols) : cols - 1;
     const int nvis = (q + VEC) / VEC;
+    const int qe = q - (nvis - 1) * VEC;
     const uint8_t* sx = ring + (size_t)s * sb;
-    const TG* sg = reinterpret_cast<const TG*>(sx + gofs);
+    const uint8_t* sg = sx + gofs;
     float sum_y = 0.f, sum_gy = 0.f;
     for (int v = lane; v < nvis; v += 32) {
-      Pack<T, VEC> p;
-      p.u = *reinterpret_cast<const uint4*>(sx + (size_t)v * 16);
+      float xf[VEC], gf[VEC];
+      unpack<T, VEC>(sx + (size_t)v * 16, xf);
+      unpack<TG, VEC>(sg + (size_t)v * GB, gf);
+      const int lim = (CAUSAL && v == nvis - 1) ? qe : VEC - 1;
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
-        if (!CAUSAL || v * VEC + e <= q) {
-          const float yy = family_y(p.get(e), alpha, theta, power);
-          sum_y += yy;
-          sum_gy += to_f<TG>(sg[v * VEC + e]) * yy;
-        }
+        const float yy = e <= lim ? y_scaled<P2>(xf[e], c1, c0, power) : 0.f;
+        sum_y += yy;
+        sum_gy = fmaf(gf[e], yy, sum_gy);
       }
     }
-    const float S = rowsum != nullptr ? __ldg(rowsum + row) : warp_sum(sum_y) + SA_EPS;
-    const float invS = 1.0f / S;
-    const float dot = warp_sum(sum_gy) * invS;
+    const float Sp = rowsum != nullptr ? __ldg(rowsum + row) * s_scale : warp_sum(sum_y) + eps_s;  // S' = 2^p S
+    const float invSp = 1.0f / Sp;
+    const float dot = warp_sum(sum_gy) * invSp;  // sum_k g_k p_k
+    const float kr = kp * (invSp * s_scale);     // kp / S
     T* drow = dx + row * ldd;
     for (int v = lane; v < nvec; v += 32) {
       Pack<T, VEC> o;
       if (v < nvis) {
-        Pack<T, VEC> p;
-        p.u = *reinterpret_cast<const uint4*>(sx + (size_t)v * 16);
+        float xf[VEC], gf[VEC];
+        unpack<T, VEC>(sx + (size_t)v * 16, xf);
+        unpack<TG, VEC>(sg + (size_t)v * GB, gf);
+        const int lim = (CAUSAL && v == nvis - 1) ? qe : VEC - 1;
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
-          float d = 0.f;
-          if (!CAUSAL || v * VEC + e <= q) {
-            const float a = alpha * (p.get(e) - theta);
-            const float u = fmaf(a, a, 4.0f);
-            const float r = rsqrtf(u);
-            const float sp = 0.5f * (a + u * r);
-            const float spp = 0.5f * fmaf(a, r, 1.0f);
-            float dydx = ap * spp;
-            if (power >= 2) dydx *= sp;
-            if (power == 3) dydx *= sp;
-            d = (dydx * invS) * (to_f<TG>(sg[v * VEC + e]) - dot);
+          const float a = fmaf(xf[e], c1, c0);
+          const float u = fmaf(a, a, 4.0f);
+          const float r = rsqrt_approx(u);
+          const float w = fmaf(a, r, 1.0f);
+          float dydx = kr * w;
+          if (P2) {
+            dydx *= fmaf(u, r, a);
+          } else if (power >= 2) {
+            const float t = fmaf(u, r, a);
+            dydx *= t;
+            if (power == 3) dydx *= t;
           }
-          o.set(e, d);
+          o.set(e, e <= lim ? dydx * (gf[e] - dot) : 0.f);
         }
       } else {
         o.zero();
@@ -572,54 +608,83 @@ static unsigned bulk_grid(K kernel, size_t smem, int64_t rows) {
   return (unsigned)(want < cap ? want : cap);
 }
 
-template <typename T, int CH, bool CAUSAL>
+struct FamConst {
+  float c1, c0, eps_s, s_scale, s_unscale, kp;
+  bool p2;
+};
+
+static FamConst fam_const(float alpha, float theta, int power) {
+  FamConst f;
+  const float two_p = (float)(1 << power);
+  f.c1 = alpha;
+  f.c0 = -alpha * theta;
+  f.eps_s = SA_EPS * two_p;
+  f.s_scale = two_p;
+  f.s_unscale = 1.0f / two_p;
+  f.kp = alpha * (float)power / two_p;
+  f.p2 = power == 2;
+  return f;
+}
+
+template <typename T, int CH, bool CAUSAL, bool P2>
 static void fwd_bulk_launch(const void* x, void* out, float* rowsum, int64_t rows, int cols, int64_t ldx,
-                            int64_t ldo, float alpha, float theta, int power, cudaStream_t st) {
+                            int64_t ldo, const FamConst& f, int power, cudaStream_t st) {
   const BulkShape b = bulk_shape(cols * (int)sizeof(T));
-  auto k = norm_fwd_bulk<T, CH, CAUSAL>;
+  auto k = norm_fwd_bulk<T, CH, CAUSAL, P2>;
   const unsigned grid = bulk_grid(k, b.smem, rows);
   k<<<grid, kBulkWarps * 32, b.smem, st>>>(static_cast<const T*>(x), static_cast<T*>(out), rowsum, rows, cols,
-                                            ldx, ldo, alpha, theta, power, b.nst, b.sb);
+                                            ldx, ldo, f.c1, f.c0, power, f.eps_s, f.s_unscale, b.nst, b.sb);
 }
 
 template <typename T, bool CAUSAL>
 static void fwd_bulk_t(const void* x, void* out, float* rowsum, int64_t rows, int cols, int64_t ldx, int64_t ldo,
                        float alpha, float theta, int power, cudaStream_t st) {
   constexpr int VEC = 16 / sizeof(T);
+  const FamConst f = fam_const(alpha, theta, power);
   const int nvec = cols / VEC;
-  const int ch = next_pow2((nvec + 31) / 32);
-#define SA_FB(CH) fwd_bulk_launch<T, CH, CAUSAL>(x, out, rowsum, rows, cols, ldx, ldo, alpha, theta, power, st)
-  if (ch * VEC > 64) { SA_FB(0); return; }
+  int ch = next_pow2((nvec + 31) / 32);
+  if (ch * VEC > 64) ch = 0;
+#define SA_FB(CH)                                                                                        \
+  do {                                                                                                   \
+    if (f.p2) fwd_bulk_launch<T, CH, CAUSAL, true>(x, out, rowsum, rows, cols, ldx, ldo, f, power, st);  \
+    else fwd_bulk_launch<T, CH, CAUSAL, false>(x, out, rowsum, rows, cols, ldx, ldo, f, power, st);      \
+  } while (0)
   switch (ch) {
     case 1: SA_FB(1); break;
     case 2: SA_FB(2); break;
     case 4: SA_FB(4); break;
     case 8: SA_FB(8); break;
-    default: if constexpr (VEC <= 4) { SA_FB(16); } else { SA_FB(0); } break;
+    case 16: if constexpr (VEC <= 4) { SA_FB(16); } else { SA_FB(0); } break;
+    default: SA_FB(0); break;
   }
 #undef SA_FB
 }
 
-template <typename T, typename TG, bool CAUSAL>
+template <typename T, typename TG, bool CAUSAL, bool P2>
 static void bwd_bulk_launch(const void* x, const void* g, const float* rowsum, void* dx, int64_t rows, int cols,
-                            int64_t ldx, int64_t ldg, int64_t ldd, float alpha, float theta, int power,
-                            cudaStream_t st) {
+                            int64_t ldx, int64_t ldg, int64_t ldd, const FamConst& f, int power, cudaStream_t st) {
   const int gofs = (cols * (int)sizeof(T) + 15) & ~15;
   const int gbytes = (cols * (int)sizeof(TG) + 15) & ~15;
   const BulkShape b = bulk_shape(gofs + gbytes);
-  auto k = norm_bwd_bulk<T, TG, CAUSAL>;
+  auto k = norm_bwd_bulk<T, TG, CAUSAL, P2>;
   const unsigned grid = bulk_grid(k, b.smem, rows);
   k<<<grid, kBulkWarps * 32, b.smem, st>>>(static_cast<const T*>(x), static_cast<const TG*>(g), rowsum,
-                                            static_cast<T*>(dx), rows, cols, ldx, ldg, ldd, alpha, theta, power,
-                                            b.nst, b.sb, gofs);
+                                            static_cast<T*>(dx), rows, cols, ldx, ldg, ldd, f.c1, f.c0, power,
+                                            f.eps_s, f.s_scale, f.kp, b.nst, b.sb, gofs);
 }
 
 template <typename T, typename TG>
 static void bwd_bulk_t(bool causal, const void* x, const void* g, const float* rowsum, void* dx, int64_t rows,
                        int cols, int64_t ldx, int64_t ldg, int64_t ldd, float alpha, float theta, int power,
                        cudaStream_t st) {
-  if (causal) bwd_bulk_launch<T, TG, true>(x, g, rowsum, dx, rows, cols, ldx, ldg, ldd, alpha, theta, power, st);
-  else bwd_bulk_launch<T, TG, false>(x, g, rowsum, dx, rows, cols, ldx, ldg, ldd, alpha, theta, power, st);
+  const FamConst f = fam_const(alpha, theta, power);
+#define SA_BB(C, P) bwd_bulk_launch<T, TG, C, P>(x, g, rowsum, dx, rows, cols, ldx, ldg, ldd, f, power, st)
+  if (causal) {
+    if (f.p2) SA_BB(true, true); else SA_BB(true, false);
+  } else {
+    if (f.p2) SA_BB(false, true); else SA_BB(false, false);
+  }
+#undef SA_BB
 }
 
 int norm_timeouts(int reset) {

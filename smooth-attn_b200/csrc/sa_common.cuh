@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/smooth_attn_b200.h"
 
 #define SA_EPS 1e-12f  // src/smooth_attn/kernels.py:57
@@ -64,6 +66,37 @@ __device__ __forceinline__ void store_stream(T* ptr, const Pack<T, VEC>& p) {
 // sqrt(u) as u * rsqrt(u): one MUFU op, the reference's `_fast_sqrt`
 // (src/smooth_attn/kernels.py:467-470).  u >= 4 here, so no 0/inf cases.
 __device__ __forceinline__ float fast_sqrt(float u) { return u * rsqrtf(u); }
+
+// Single-instruction approximate reciprocal square root (MUFU), flushing
+// denormals: every argument here is u = a*a + 4 >= 4, so no special cases.
+__device__ __forceinline__ float rsqrt_approx(float u) {
+  float r;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(u));
+  return r;
+}
+
+// Unpack VEC elements of a 16-byte pack (or 8 bytes) into floats.
+template <typename T, int N>
+__device__ __forceinline__ void unpack(const void* src, float (&out)[N]) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = reinterpret_cast<const float*>(src)[i];
+  } else {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(src);
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        out[2 * i] = __uint_as_float(w[i] << 16);
+        out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        const float2 f = __half22float2(h);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+      }
+    }
+  }
+}
 
 }  // namespace sa
 
