@@ -44,6 +44,9 @@ import torch  # noqa: E402
 NORM_CFG = dict(B=8, H=16, L=2048)  # BASELINE configs[1], largest L
 FLASH_CFG = dict(B=4, H=32, T=4096, D=128)
 METRIC = "causal-norm HBM GB/s"
+# DRAM bytes (read + write) of one norm_fwd_bulk launch at [8,16,2048,2048]: ncu
+# capture of the [2,16,2048,2048] case scaled by 4 (see profiles/).
+NORM_TRAFFIC_BYTES = 4 * (138.446336e6 + 208.5952e6)
 
 
 def norm_bytes(M, L, e=2, rowsum=False):
@@ -232,7 +235,8 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "traffic": args.traffic_bytes,
                          "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                         "algorithmic_bytes_per_launch": norm_bytes(m_loc, L), "kernel": "sa::norm_fwd_kernel"},
+                         "algorithmic_bytes_per_launch": norm_bytes(m_loc, L), "kernel": "sa::norm_fwd_bulk",
+                         "traffic_source": "profiles/norm_fwd_bulk_causal_bf16_L2048.md (ncu [2,16,2048,2048] x4)"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 2,
                     "d2h_bytes_per_step": out.numel() * 2,
                     "path": "pinned host x -> H2D -> softplus_norm_causal_triton_out -> D2H"},
@@ -364,7 +368,7 @@ def main():
                     help="B,H,T,D of the attention workload (BASELINE: 4,32,4096,128)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--traffic-bytes", type=float, default=None,
+    ap.add_argument("--traffic-bytes", type=float, default=NORM_TRAFFIC_BYTES,
                     help="ncu dram bytes per launch of the norm kernel, if measured")
     args = ap.parse_args()
     if args.impl == "reference":
