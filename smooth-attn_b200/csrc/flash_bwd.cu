@@ -453,7 +453,8 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
   uint32_t sv[32], dv[32];
   tmem_ld32(tS + 32 * w2, sv);
   tmem_ld32(tP + 32 * w2, dv);
-  tmem_ld_wait();
+  tmem_ld_wait(sv);
+  tmem_ld_wait(dv);
   uint32_t pk[16], dk[16];
 #pragma unroll
   for (int e = 0; e < 32; e += 4) {
@@ -486,9 +487,9 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
     dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
     dk[e / 2 + 1] = BF16 ? pack2_bf16(dsv[2], dsv[3]) : pack2_f16(dsv[2], dsv[3]);
   }
-  // both warpgroups must have read their S^T columns before P overwrites them
-  ew_sync();
-  tmem_st16(tS + 16 * w2, pk);
+  // P of query columns [32 w2, 32 w2 + 32) goes over this warpgroup's own,
+  // already-read S^T columns [32 w2, 32 w2 + 16): no cross-warpgroup hazard.
+  tmem_st16(tS + 32 * w2, pk);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int piece = (w2 * 4 + j) ^ (r & 7);
@@ -625,7 +626,8 @@ __global__ void __launch_bounds__(448, 1)
             const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
             const uint64_t b_do = smem_desc(do_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
             const uint64_t b_q = smem_desc(q_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
-            mma_ts(tDV, tbase + bb * 64 + kk * 8, b_do, id_kv, acc);
+            // P of query rows [16 kk, 16 kk + 16) sits at columns 32 (kk / 2) + 8 (kk % 2)
+            mma_ts(tDV, tbase + bb * 64 + (kk >> 1) * 32 + (kk & 1) * 8, b_do, id_kv, acc);
             mma_ss(tDK, smem_desc(ds_s + kk * 32, 16, 1024, SW_128B), b_q, id_kv, acc);
           }
 #pragma unroll

@@ -109,14 +109,11 @@ __device__ __forceinline__ void kv_range(int q0, int T, int window, int& j0, int
   if (q0 >= T) j1 = j0;  // tile wholly past the sequence end: no work
 }
 
-// One 32-column chunk of squareplus on a score row held in TMEM; writes the
-// bf16/f16 P back over the chunk's first 16 columns and returns sum(y').
+// squareplus of one 32-column chunk already in registers; writes the
+// bf16/f16 P over the chunk's first 16 TMEM columns and returns sum(y').
 template <bool BF16, bool EXACT, bool MASK>
-__device__ __forceinline__ float squareplus_chunk(uint32_t taddr_s, uint32_t taddr_p, float scale2, int kbase, int q,
-                                                  int T, int window) {
-  uint32_t r[32];
-  tmem_ld32(taddr_s, r);
-  tmem_ld_wait();
+__device__ __forceinline__ float squareplus_regs(const uint32_t (&r)[32], uint32_t taddr_p, float scale2, int kbase,
+                                                 int q, int T, int window) {
   uint32_t pk[16];
   float sum = 0.f;
 #pragma unroll
@@ -139,6 +136,27 @@ __device__ __forceinline__ float squareplus_chunk(uint32_t taddr_s, uint32_t tad
     pk[e / 2] = BF16 ? pack2_bf16(yv[0], yv[1]) : pack2_f16(yv[0], yv[1]);
   }
   tmem_st16(taddr_p, pk);
+  return sum;
+}
+
+// One 128-column score row: TMEM loads run one chunk ahead of the math
+// (two register buffers), so the load latency hides behind the previous
+// chunk's squareplus.  P for chunk c goes to columns [16c, 16c+16), which
+// hold only already-loaded scores.
+template <bool BF16, bool EXACT, bool MASK>
+__device__ __forceinline__ float squareplus_row(uint32_t tS, float scale2, int k0, int q, int T, int window) {
+  uint32_t ra[32], rb[32];
+  float sum = 0.f;
+  tmem_ld32(tS, ra);
+#pragma unroll 1
+  for (int c = 0; c < 4; c += 2) {
+    tmem_ld_wait(ra);
+    tmem_ld32(tS + (c + 1) * 32, rb);
+    sum += squareplus_regs<BF16, EXACT, MASK>(ra, tS + c * 16, scale2, k0 + c * 32, q, T, window);
+    tmem_ld_wait(rb);
+    if (c + 2 < 4) tmem_ld32(tS + (c + 2) * 32, ra);
+    sum += squareplus_regs<BF16, EXACT, MASK>(rb, tS + (c + 1) * 16, scale2, k0 + (c + 1) * 32, q, T, window);
+  }
   return sum;
 }
 
@@ -316,15 +334,10 @@ __global__ void __launch_bounds__(320, 1)
       const int k0 = j * C::BN;
       const bool need_mask = (k0 + C::BN - 1 > q0) || (k0 + C::BN > p.T) ||
                              (p.window > 0 && q0 + C::BM - 1 - k0 >= p.window);
-      if (need_mask) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c)
-          rsum += squareplus_chunk<BF16, EXACT, true>(tS + c * 32, tS + c * 16, p.scale2, k0 + c * 32, q, p.T, p.window);
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c)
-          rsum += squareplus_chunk<BF16, EXACT, false>(tS + c * 32, tS + c * 16, p.scale2, 0, 0, 0, 0);
-      }
+      if (need_mask)
+        rsum += squareplus_row<BF16, EXACT, true>(tS, p.scale2, k0, q, p.T, p.window);
+      else
+        rsum += squareplus_row<BF16, EXACT, false>(tS, p.scale2, 0, 0, 0, 0);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->p_full[t]);
