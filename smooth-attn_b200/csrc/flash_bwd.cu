@@ -398,11 +398,12 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------
 // D = 128 backward: 64-row query tiles, double-buffered S^T / dP^T in TMEM.
 //
-// TMEM (512 columns): S^T_b @ 64b, dP^T_b (later dQ^T_b) @ 128 + 64b,
+// TMEM (512 columns): S^T_b @ 64b (double-buffered), dP^T @ 128, dQ^T @ 192,
 // dK @ 256, dV @ 384.  dQ is produced transposed, dQ^T = K^T dS^T (M = the
-// 128 head-dim rows, N = 64 query columns), into the dP^T columns the
-// elementwise stage has just consumed, so every accumulator fits and the
-// S/dP MMAs of tile i+1 run while tile i's elementwise stage runs.
+// 128 head-dim rows, N = 64 query columns), so it needs only 64 columns.
+// S^T(i+2) and dP^T(i+1) are issued as soon as their buffers are free, so
+// the tensor pipe works on the next tiles while tile i's elementwise stage
+// and dQ drain run; the drain of tile i only gates dQ^T(i+1).
 // Warps: 0-7 elementwise (two warpgroups, 32 query columns each), 8-11 dQ
 // drain (TMEM lane = head-dim index: coalesced fp32 atomics), 12 TMA, 13 MMA.
 // ---------------------------------------------------------------------------
@@ -425,7 +426,12 @@ struct Bwd128 {
 struct Bwd128Bars {
   uint64_t kv_full;
   uint64_t q_full[3], q_empty[3];
-  uint64_t s_full[2], p_ready[2], mm2_done[2], dq_free[2];
+  uint64_t s_full[2];  // S^T of tile j ready in buffer j&1
+  uint64_t dp_full;    // dP^T of tile j ready (single buffer)
+  uint64_t p_ready;    // elementwise stage of tile j done (256 arrivals)
+  uint64_t dv_done;    // dV(j) complete: S^T buffer j&1 may be overwritten
+  uint64_t mm2_done;   // dK(j), dQ^T(j) complete
+  uint64_t dq_free;    // dQ^T(j) read out of TMEM (128 arrivals)
   uint64_t all_done;
   uint32_t tmem_base;
 };
@@ -535,12 +541,12 @@ __global__ void __launch_bounds__(448, 1)
       mbar_init(&bars->q_full[i], 1);
       mbar_init(&bars->q_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_ready[i], 256);
-      mbar_init(&bars->mm2_done[i], 1);
-      mbar_init(&bars->dq_free[i], 128);
-    }
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->s_full[i], 1);
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->p_ready, 256);
+    mbar_init(&bars->dv_done, 1);
+    mbar_init(&bars->mm2_done, 1);
+    mbar_init(&bars->dq_free, 128);
     mbar_init(&bars->all_done, 1);
     fence_mbar_init();
   }
@@ -588,56 +594,75 @@ __global__ void __launch_bounds__(448, 1)
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
       const uint32_t aDS = smem_u32(sDS);
       const uint32_t tDK = tbase + 256, tDV = tbase + 384;
-      auto issue_sdp = [&](int it) {
-        const int st = it % C::NS, bb = it & 1;
-        const uint32_t q_s = aQ + st * C::Q_TILE, do_s = aDO + st * C::Q_TILE;
+      auto issue_s = [&](int it) {  // S^T(it) = K Q^T -> buffer it&1
+        const uint32_t q_s = aQ + (it % C::NS) * C::Q_TILE;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;  // K/V: 128-row chunks
-          const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;  // Q/dO: 64-row chunks
-          mma_ss(tbase + bb * 64, smem_desc(aK + koff, 16, 1024, SW_128B), smem_desc(q_s + qoff, 16, 1024, SW_128B),
-                 id_s, kk > 0);
-          mma_ss(tbase + 128 + bb * 64, smem_desc(aV + koff, 16, 1024, SW_128B),
-                 smem_desc(do_s + qoff, 16, 1024, SW_128B), id_s, kk > 0);
+          const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;  // K: 128-row chunks
+          const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;  // Q: 64-row chunks
+          mma_ss(tbase + (it & 1) * 64, smem_desc(aK + koff, 16, 1024, SW_128B),
+                 smem_desc(q_s + qoff, 16, 1024, SW_128B), id_s, kk > 0);
         }
-        mma_commit(&bars->s_full[bb]);
+        mma_commit(&bars->s_full[it & 1]);
       };
+      auto issue_dp = [&](int it) {  // dP^T(it) = V dO^T -> the dP^T buffer
+        const uint32_t do_s = aDO + (it % C::NS) * C::Q_TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;
+          const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;
+          mma_ss(tbase + 128, smem_desc(aV + koff, 16, 1024, SW_128B), smem_desc(do_s + qoff, 16, 1024, SW_128B),
+                 id_s, kk > 0);
+        }
+        mma_commit(&bars->dp_full);
+      };
+      // Order per tile j: [elementwise(j) done] dP(j+1), dV(j), dK(j),
+      // [drain(j-1) done] dQ(j), [dV(j) done] S(j+2).  The dQ drain of one
+      // tile overlaps the next tile's MMAs; only dQ(j) itself waits for it.
       if (b_wait(&bars->kv_full, 0, failed) && ntiles > 0 && b_wait(&bars->q_full[0], 0, failed)) {
         tc_fence_after();
-        issue_sdp(0);
+        issue_s(0);
+        issue_dp(0);
+        if (ntiles > 1 && b_wait(&bars->q_full[1], 0, failed)) {
+          tc_fence_after();
+          issue_s(1);
+        }
         for (int it = 0; it < ntiles && !failed; ++it) {
           const int bb = it & 1, st = it % C::NS;
-          if (it + 1 < ntiles) {
-            const int nx = it + 1;
-            if (!b_wait(&bars->q_full[nx % C::NS], (nx / C::NS) & 1, failed)) break;
-            if (it >= 1) {
-              if (!b_wait(&bars->mm2_done[bb ^ 1], ((it - 1) >> 1) & 1, failed)) break;
-              if (!b_wait(&bars->dq_free[bb ^ 1], ((it - 1) >> 1) & 1, failed)) break;
-            }
-            tc_fence_after();
-            issue_sdp(nx);
-          }
-          if (!b_wait(&bars->p_ready[bb], (it >> 1) & 1, failed)) break;
+          if (!b_wait(&bars->p_ready, it & 1, failed)) break;
           tc_fence_after();
+          if (it + 1 < ntiles) issue_dp(it + 1);
           const uint32_t q_s = aQ + st * C::Q_TILE, do_s = aDO + st * C::Q_TILE;
           const uint32_t ds_s = aDS + bb * C::DS_TILE;
 #pragma unroll
-          for (int kk = 0; kk < C::BQ / 16; ++kk) {  // K = 64 query rows
-            const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          for (int kk = 0; kk < C::BQ / 16; ++kk) {  // dV += P^T dO, K = 64 query rows
             const uint64_t b_do = smem_desc(do_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
-            const uint64_t b_q = smem_desc(q_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
             // P of query rows [16 kk, 16 kk + 16) sits at columns 32 (kk / 2) + 8 (kk % 2)
-            mma_ts(tDV, tbase + bb * 64 + (kk >> 1) * 32 + (kk & 1) * 8, b_do, id_kv, acc);
-            mma_ss(tDK, smem_desc(ds_s + kk * 32, 16, 1024, SW_128B), b_q, id_kv, acc);
+            mma_ts(tDV, tbase + bb * 64 + (kk >> 1) * 32 + (kk & 1) * 8, b_do, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
           }
+          mma_commit(&bars->dv_done);
 #pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk) {  // K = 128 KV rows
+          for (int kk = 0; kk < C::BQ / 16; ++kk) {  // dK += dS^T Q
+            const uint64_t b_q = smem_desc(q_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
+            mma_ss(tDK, smem_desc(ds_s + kk * 32, 16, 1024, SW_128B), b_q, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (it >= 1 && !b_wait(&bars->dq_free, (it - 1) & 1, failed)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk) {  // dQ^T = K^T dS^T, K = 128 KV rows
             const uint64_t a_kt = smem_desc(aK + kk * 16 * 128, 128 * 128, 1024, SW_128B);
             const uint64_t b_ds = smem_desc(ds_s + kk * 16 * 128, C::DS_TILE, 1024, SW_128B);
-            mma_ss(tbase + 128 + bb * 64, a_kt, b_ds, id_dq, kk > 0);
+            mma_ss(tbase + 192, a_kt, b_ds, id_dq, kk > 0);
           }
-          mma_commit(&bars->mm2_done[bb]);
+          mma_commit(&bars->mm2_done);
           mma_commit(&bars->q_empty[st]);
+          if (it + 2 < ntiles) {
+            const int nx = it + 2;
+            if (!b_wait(&bars->q_full[nx % C::NS], (nx / C::NS) & 1, failed)) break;
+            if (!b_wait(&bars->dv_done, it & 1, failed)) break;
+            tc_fence_after();
+            issue_s(nx);
+          }
         }
       }
       mma_commit(&bars->all_done);
@@ -648,15 +673,15 @@ __global__ void __launch_bounds__(448, 1)
     const int d = 32 * g + lane;  // TMEM lane = head-dim index of dQ^T
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     for (int it = 0; it < ntiles && !failed; ++it) {
-      const int bb = it & 1;
-      if (!b_warp_wait(&bars->mm2_done[bb], (it >> 1) & 1, failed)) break;
+      if (!b_warp_wait(&bars->mm2_done, it & 1, failed)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
-      tmem_ld32(tl + 128 + bb * 64, v0);
-      tmem_ld32(tl + 128 + bb * 64 + 32, v1);
-      tmem_ld_wait();
+      tmem_ld32(tl + 192, v0);
+      tmem_ld32(tl + 224, v1);
+      tmem_ld_wait(v0);
+      tmem_ld_wait(v1);
       tc_fence_before();
-      mbar_arrive(&bars->dq_free[bb]);
+      mbar_arrive(&bars->dq_free);
       const int h = kvh * G + it / per_head;
       const int q0 = (qt_first + it % per_head) * C::BQ;
       float* dst = p.dq_acc + (((int64_t)b * p.Hq + h) * p.T + q0) * D + d;
@@ -695,7 +720,7 @@ __global__ void __launch_bounds__(448, 1)
       ew_sync();
       prefetch(it + 1);
       // all 256 threads leave together on a timeout (the chunk below has a named barrier)
-      if (!ew_all(mbar_wait(&bars->s_full[bb], (it >> 1) & 1))) {
+      if (!ew_all(mbar_wait(&bars->s_full[bb], (it >> 1) & 1) && mbar_wait(&bars->dp_full, it & 1))) {
         if (tid == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
         failed = true;
         break;
@@ -705,15 +730,15 @@ __global__ void __launch_bounds__(448, 1)
                              (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
       uint8_t* dsrow = sDS + bb * C::DS_TILE + r * 128;
       if (need_mask)
-        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
+        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128, w2, dsrow, r, vInvR + bb * 64,
                                         vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
       else
-        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
+        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128, w2, dsrow, r, vInvR + bb * 64,
                                          vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->p_ready[bb]);
+      mbar_arrive(&bars->p_ready);
     }
     // epilogue: warpgroup 0 writes dK, warpgroup 1 writes dV (TMEM lane = KV row)
     if (b_warp_wait(&bars->all_done, 0, failed)) {
