@@ -594,25 +594,26 @@ __global__ void __launch_bounds__(448, 1)
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
       const uint32_t aDS = smem_u32(sDS);
       const uint32_t tDK = tbase + 256, tDV = tbase + 384;
+      // descriptors are built once and advanced with plain adds in the MMA loops
+      const uint64_t dK0 = smem_desc(aK, 16, 1024, SW_128B), dV0 = smem_desc(aV, 16, 1024, SW_128B);
+      const uint64_t dKt0 = smem_desc(aK, 128 * 128, 1024, SW_128B);  // K as MN-major A (K^T)
       auto issue_s = [&](int it) {  // S^T(it) = K Q^T -> buffer it&1
-        const uint32_t q_s = aQ + (it % C::NS) * C::Q_TILE;
+        const uint64_t dq0 = smem_desc(aQ + (it % C::NS) * C::Q_TILE, 16, 1024, SW_128B);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;  // K: 128-row chunks
           const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;  // Q: 64-row chunks
-          mma_ss(tbase + (it & 1) * 64, smem_desc(aK + koff, 16, 1024, SW_128B),
-                 smem_desc(q_s + qoff, 16, 1024, SW_128B), id_s, kk > 0);
+          mma_ss(tbase + (it & 1) * 64, desc_add(dK0, koff), desc_add(dq0, qoff), id_s, kk > 0);
         }
         mma_commit(&bars->s_full[it & 1]);
       };
       auto issue_dp = [&](int it) {  // dP^T(it) = V dO^T -> the dP^T buffer
-        const uint32_t do_s = aDO + (it % C::NS) * C::Q_TILE;
+        const uint64_t ddo0 = smem_desc(aDO + (it % C::NS) * C::Q_TILE, 16, 1024, SW_128B);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;
           const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;
-          mma_ss(tbase + 128, smem_desc(aV + koff, 16, 1024, SW_128B), smem_desc(do_s + qoff, 16, 1024, SW_128B),
-                 id_s, kk > 0);
+          mma_ss(tbase + 128, desc_add(dV0, koff), desc_add(ddo0, qoff), id_s, kk > 0);
         }
         mma_commit(&bars->dp_full);
       };
@@ -634,25 +635,26 @@ __global__ void __launch_bounds__(448, 1)
           if (it + 1 < ntiles) issue_dp(it + 1);
           const uint32_t q_s = aQ + st * C::Q_TILE, do_s = aDO + st * C::Q_TILE;
           const uint32_t ds_s = aDS + bb * C::DS_TILE;
+          const uint64_t bdo0 = smem_desc(do_s, C::BQ * 128, 1024, SW_128B);
+          const uint64_t bq0 = smem_desc(q_s, C::BQ * 128, 1024, SW_128B);
+          const uint64_t ads0 = smem_desc(ds_s, 16, 1024, SW_128B);
+          const uint64_t bds0 = smem_desc(ds_s, C::DS_TILE, 1024, SW_128B);
 #pragma unroll
           for (int kk = 0; kk < C::BQ / 16; ++kk) {  // dV += P^T dO, K = 64 query rows
-            const uint64_t b_do = smem_desc(do_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
+            const uint64_t b_do = desc_add(bdo0, kk * 16 * 128);
             // P of query rows [16 kk, 16 kk + 16) sits at columns 32 (kk / 2) + 8 (kk % 2)
             mma_ts(tDV, tbase + bb * 64 + (kk >> 1) * 32 + (kk & 1) * 8, b_do, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&bars->dv_done);
 #pragma unroll
           for (int kk = 0; kk < C::BQ / 16; ++kk) {  // dK += dS^T Q
-            const uint64_t b_q = smem_desc(q_s + kk * 16 * 128, C::BQ * 128, 1024, SW_128B);
-            mma_ss(tDK, smem_desc(ds_s + kk * 32, 16, 1024, SW_128B), b_q, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+            mma_ss(tDK, desc_add(ads0, kk * 32), desc_add(bq0, kk * 16 * 128), id_kv, (it > 0 || kk > 0) ? 1u : 0u);
           }
           if (it >= 1 && !b_wait(&bars->dq_free, (it - 1) & 1, failed)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < C::BN / 16; ++kk) {  // dQ^T = K^T dS^T, K = 128 KV rows
-            const uint64_t a_kt = smem_desc(aK + kk * 16 * 128, 128 * 128, 1024, SW_128B);
-            const uint64_t b_ds = smem_desc(ds_s + kk * 16 * 128, C::DS_TILE, 1024, SW_128B);
-            mma_ss(tbase + 192, a_kt, b_ds, id_dq, kk > 0);
+            mma_ss(tbase + 192, desc_add(dKt0, kk * 16 * 128), desc_add(bds0, kk * 16 * 128), id_dq, kk > 0);
           }
           mma_commit(&bars->mm2_done);
           mma_commit(&bars->q_empty[st]);

@@ -243,14 +243,16 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
       const int jlo[2] = {ja0, jb0}, jhi[2] = {ja1, jb1};
       int s_cnt[2] = {0, 0}, pv_cnt[2] = {0, 0};
+      // descriptors are built once and advanced with plain adds in the MMA loops
+      const uint64_t dQ0 = smem_desc(aQ, 16, C::SBO, C::SWZ), dK0 = smem_desc(aK, 16, C::SBO, C::SWZ);
+      const uint64_t dV0 = smem_desc(aV, 128 * C::ROWB, C::SBO, C::SWZ);
       auto issue_s = [&](int t, int i) {
         const int ks = i % C::NK;
-        const uint32_t q_s = aQ + t * C::TILE, k_s = aK + ks * C::TILE;
+        const uint64_t dq0 = desc_add(dQ0, t * C::TILE), dk0 = desc_add(dK0, ks * C::TILE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = ((kk * 16) / C::CHUNK) * 128 * C::ROWB + ((kk * 16) % C::CHUNK) * 2;
-          mma_ss(tbase + t * 128, smem_desc(q_s + off, 16, C::SBO, C::SWZ), smem_desc(k_s + off, 16, C::SBO, C::SWZ),
-                 idesc_s, kk > 0);
+          mma_ss(tbase + t * 128, desc_add(dq0, off), desc_add(dk0, off), idesc_s, kk > 0);
         }
         mma_commit(&bars->s_full[t]);
         ++s_cnt[t];
@@ -274,10 +276,10 @@ __global__ void __launch_bounds__(320, 1)
             // O_t += P_t V_j once the squareplus warps have written P_t
             if (!wait_or_flag(&bars->p_full[t], (pv_cnt[t]) & 1, failed)) break;
             tc_fence_after();
-            const uint32_t v_s = aV + vs * C::TILE;
+            const uint64_t dv0 = desc_add(dV0, vs * C::TILE);
 #pragma unroll
             for (int kk = 0; kk < C::BN / 16; ++kk) {
-              const uint64_t db = smem_desc(v_s + kk * 16 * C::ROWB, 128 * C::ROWB, C::SBO, C::SWZ);
+              const uint64_t db = desc_add(dv0, kk * 16 * C::ROWB);
               mma_ts(tbase + 256 + t * D, tbase + t * 128 + kk * 8, db, idesc_o, (j > jlo[t] || kk > 0) ? 1u : 0u);
             }
             mma_commit(&bars->pv_done[t]);

@@ -71,6 +71,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
+// Advance a descriptor's start address by `bytes` (a multiple of 16): the
+// start field is the low 14 bits of (address >> 4) and shared-memory
+// addresses stay below 2^18, so a plain add never carries out of the field.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (uint64_t)(bytes >> 4); }
+
 // kind::f16 instruction descriptor: fp32 accumulate, A/B both f16 (ab=0) or bf16 (ab=1).
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_bf16, int a_mn_major, int b_mn_major) {
   return (1u << 4) | ((uint32_t)ab_bf16 << 7) | ((uint32_t)ab_bf16 << 10) | ((uint32_t)a_mn_major << 15) |
