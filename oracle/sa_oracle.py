@@ -88,6 +88,20 @@ def softplus_norm_causal(x, alpha=2.0, theta=0.5, power=2, acc=np.float32, retur
     return out
 
 
+def softplus_norm_causal_rows(x_rows, q0, alpha=2.0, theta=0.5, power=2, acc=np.float32):
+    """Causal normalization of a block of rows of one [L, L] score matrix.
+
+    x_rows: [n, L] holding query positions q0 .. q0+n-1; column j is visible
+    to query q iff j <= q (the row test ``q_pos = row % L`` of kernels.py:585).
+    """
+    x_rows = _as_f(x_rows, acc)
+    n, L = x_rows.shape
+    q = np.arange(q0, q0 + n)[:, None]
+    vis = np.arange(L)[None, :] <= q
+    y = np.where(vis, family_activation(x_rows, alpha, theta, power, acc), acc(0.0))
+    return y / (y.sum(axis=-1, keepdims=True) + acc(EPS))
+
+
 def softplus_norm_causal_bwd(x, g, alpha=2.0, theta=0.5, power=2, acc=np.float32):
     """Gradient of ``sum(softplus_norm_causal(x) * g)`` w.r.t. x.
 
