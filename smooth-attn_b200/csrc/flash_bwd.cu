@@ -47,7 +47,7 @@ namespace {
 
 __device__ __forceinline__ bool b_wait(uint64_t* bar, uint32_t phase, bool& failed) {
   if (failed) return false;
-  if (!mbar_wait(bar, phase)) {
+  if (!mbar_wait_spin(bar, phase)) {
     failed = true;
     atomicAdd(&g_flash_bwd_timeouts, 1u);
     return false;
@@ -398,12 +398,11 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------
 // D = 128 backward: 64-row query tiles, double-buffered S^T / dP^T in TMEM.
 //
-// TMEM (512 columns): S^T_b @ 64b (double-buffered), dP^T @ 128, dQ^T @ 192,
-// dK @ 256, dV @ 384.  dQ is produced transposed, dQ^T = K^T dS^T (M = the
-// 128 head-dim rows, N = 64 query columns), so it needs only 64 columns.
-// S^T(i+2) and dP^T(i+1) are issued as soon as their buffers are free, so
-// the tensor pipe works on the next tiles while tile i's elementwise stage
-// and dQ drain run; the drain of tile i only gates dQ^T(i+1).
+// TMEM (512 columns): S^T_b @ 64b and dP^T_b @ 128 + 64b (both double-
+// buffered), dK @ 256, dV @ 384.  dQ is produced transposed, dQ^T = K^T dS^T
+// (M = the 128 head-dim rows, N = 64 query columns), into the dP^T buffer of
+// its own tile after the elementwise stage consumed it, so everything fits.
+// S^T and dP^T of tile i+2 are issued while tile i+1's elementwise stage runs.
 // Warps: 0-7 elementwise (two warpgroups, 32 query columns each), 8-11 dQ
 // drain (TMEM lane = head-dim index: coalesced fp32 atomics), 12 TMA, 13 MMA.
 // ---------------------------------------------------------------------------
@@ -426,12 +425,11 @@ struct Bwd128 {
 struct Bwd128Bars {
   uint64_t kv_full;
   uint64_t q_full[3], q_empty[3];
-  uint64_t s_full[2];  // S^T of tile j ready in buffer j&1
-  uint64_t dp_full;    // dP^T of tile j ready (single buffer)
+  uint64_t s_full[2];   // S^T of tile j ready in buffer j&1
+  uint64_t dp_full[2];  // dP^T of tile j ready in buffer j&1
   uint64_t p_ready;    // elementwise stage of tile j done (256 arrivals)
-  uint64_t dv_done;    // dV(j) complete: S^T buffer j&1 may be overwritten
   uint64_t mm2_done;   // dK(j), dQ^T(j) complete
-  uint64_t dq_free;    // dQ^T(j) read out of TMEM (128 arrivals)
+  uint64_t dq_free;    // dQ^T(j) read out of TMEM (128 arrivals): dP^T buffer j&1 free
   uint64_t all_done;
   uint32_t tmem_base;
 };
@@ -542,9 +540,8 @@ __global__ void __launch_bounds__(448, 1)
       mbar_init(&bars->q_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) mbar_init(&bars->s_full[i], 1);
-    mbar_init(&bars->dp_full, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->dp_full[i], 1);
     mbar_init(&bars->p_ready, 256);
-    mbar_init(&bars->dv_done, 1);
     mbar_init(&bars->mm2_done, 1);
     mbar_init(&bars->dq_free, 128);
     mbar_init(&bars->all_done, 1);
@@ -607,19 +604,21 @@ __global__ void __launch_bounds__(448, 1)
         }
         mma_commit(&bars->s_full[it & 1]);
       };
-      auto issue_dp = [&](int it) {  // dP^T(it) = V dO^T -> the dP^T buffer
+      auto issue_dp = [&](int it) {  // dP^T(it) = V dO^T -> dP^T buffer it&1
         const uint64_t ddo0 = smem_desc(aDO + (it % C::NS) * C::Q_TILE, 16, 1024, SW_128B);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;
           const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;
-          mma_ss(tbase + 128, desc_add(dV0, koff), desc_add(ddo0, qoff), id_s, kk > 0);
+          mma_ss(tbase + 128 + (it & 1) * 64, desc_add(dV0, koff), desc_add(ddo0, qoff), id_s, kk > 0);
         }
-        mma_commit(&bars->dp_full);
+        mma_commit(&bars->dp_full[it & 1]);
       };
-      // Order per tile j: [elementwise(j) done] dP(j+1), dV(j), dK(j),
-      // [drain(j-1) done] dQ(j), [dV(j) done] S(j+2).  The dQ drain of one
-      // tile overlaps the next tile's MMAs; only dQ(j) itself waits for it.
+      // Per tile j, once its elementwise stage is done: dV(j), dK(j), dQ^T(j)
+      // into the dP^T buffer elementwise(j) consumed, then for tile j+2: S^T
+      // (in issue order after dV(j), which reads P(j) from the same columns)
+      // and, once dQ^T(j) is drained, dP^T.  S^T and dP^T of tile j+1 were
+      // issued a tile earlier, so elementwise(j+1) starts without waiting.
       if (b_wait(&bars->kv_full, 0, failed) && ntiles > 0 && b_wait(&bars->q_full[0], 0, failed)) {
         tc_fence_after();
         issue_s(0);
@@ -627,12 +626,12 @@ __global__ void __launch_bounds__(448, 1)
         if (ntiles > 1 && b_wait(&bars->q_full[1], 0, failed)) {
           tc_fence_after();
           issue_s(1);
+          issue_dp(1);
         }
         for (int it = 0; it < ntiles && !failed; ++it) {
           const int bb = it & 1, st = it % C::NS;
           if (!b_wait(&bars->p_ready, it & 1, failed)) break;
           tc_fence_after();
-          if (it + 1 < ntiles) issue_dp(it + 1);
           const uint32_t q_s = aQ + st * C::Q_TILE, do_s = aDO + st * C::Q_TILE;
           const uint32_t ds_s = aDS + bb * C::DS_TILE;
           const uint64_t bdo0 = smem_desc(do_s, C::BQ * 128, 1024, SW_128B);
@@ -645,25 +644,26 @@ __global__ void __launch_bounds__(448, 1)
             // P of query rows [16 kk, 16 kk + 16) sits at columns 32 (kk / 2) + 8 (kk % 2)
             mma_ts(tDV, tbase + bb * 64 + (kk >> 1) * 32 + (kk & 1) * 8, b_do, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(&bars->dv_done);
 #pragma unroll
           for (int kk = 0; kk < C::BQ / 16; ++kk) {  // dK += dS^T Q
             mma_ss(tDK, desc_add(ads0, kk * 32), desc_add(bq0, kk * 16 * 128), id_kv, (it > 0 || kk > 0) ? 1u : 0u);
           }
-          if (it >= 1 && !b_wait(&bars->dq_free, (it - 1) & 1, failed)) break;
-          tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk) {  // dQ^T = K^T dS^T, K = 128 KV rows
-            mma_ss(tbase + 192, desc_add(dKt0, kk * 16 * 128), desc_add(bds0, kk * 16 * 128), id_dq, kk > 0);
+          for (int kk = 0; kk < C::BN / 16; ++kk) {  // dQ^T = K^T dS^T into dP^T buffer bb (consumed)
+            mma_ss(tbase + 128 + bb * 64, desc_add(dKt0, kk * 16 * 128), desc_add(bds0, kk * 16 * 128), id_dq, kk > 0);
           }
           mma_commit(&bars->mm2_done);
           mma_commit(&bars->q_empty[st]);
           if (it + 2 < ntiles) {
             const int nx = it + 2;
             if (!b_wait(&bars->q_full[nx % C::NS], (nx / C::NS) & 1, failed)) break;
-            if (!b_wait(&bars->dv_done, it & 1, failed)) break;
             tc_fence_after();
+            // S^T(nx) overwrites the columns dV(it) reads P from: tcgen05.mma
+            // ops of one thread execute in issue order, so no wait is needed.
             issue_s(nx);
+            if (!b_wait(&bars->dq_free, it & 1, failed)) break;
+            tc_fence_after();
+            issue_dp(nx);
           }
         }
       }
@@ -678,8 +678,8 @@ __global__ void __launch_bounds__(448, 1)
       if (!b_warp_wait(&bars->mm2_done, it & 1, failed)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
-      tmem_ld32(tl + 192, v0);
-      tmem_ld32(tl + 224, v1);
+      tmem_ld32(tl + 128 + (it & 1) * 64, v0);  // dQ^T(it) sits in dP^T buffer it&1
+      tmem_ld32(tl + 128 + (it & 1) * 64 + 32, v1);
       tmem_ld_wait(v0);
       tmem_ld_wait(v1);
       tc_fence_before();
@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(448, 1)
       ew_sync();
       prefetch(it + 1);
       // all 256 threads leave together on a timeout (the chunk below has a named barrier)
-      if (!ew_all(mbar_wait(&bars->s_full[bb], (it >> 1) & 1) && mbar_wait(&bars->dp_full, it & 1))) {
+      if (!ew_all(mbar_wait(&bars->s_full[bb], (it >> 1) & 1) && mbar_wait(&bars->dp_full[bb], (it >> 1) & 1))) {
         if (tid == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
         failed = true;
         break;
@@ -732,10 +732,10 @@ __global__ void __launch_bounds__(448, 1)
                              (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
       uint8_t* dsrow = sDS + bb * C::DS_TILE + r * 128;
       if (need_mask)
-        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128, w2, dsrow, r, vInvR + bb * 64,
+        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
                                         vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
       else
-        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128, w2, dsrow, r, vInvR + bb * 64,
+        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
                                          vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
       tmem_st_wait();
       fence_proxy_async_smem();

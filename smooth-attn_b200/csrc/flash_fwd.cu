@@ -291,8 +291,8 @@ __global__ void __launch_bounds__(320, 1)
                 if (!wait_or_flag(&bars->k_full[(i + 1) % C::NK], ((i + 1) / C::NK) & 1, failed)) break;
                 k_next_ready = true;
               }
-              if (!wait_or_flag(&bars->pv_done[t], (pv_cnt[t] - 1) & 1, failed)) break;
-              tc_fence_after();
+              // S_t overwrites the columns PV_t reads P_t from: tcgen05.mma ops
+              // of one thread execute in issue order, so no wait is needed.
               issue_s(t, i + 1);
             }
           }

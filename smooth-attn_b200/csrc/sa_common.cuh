@@ -159,6 +159,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint64_
   return true;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that polls without suspending the thread: lower wake-up
+// latency for single issuing threads (TMA / MMA) whose reaction time is on
+// the critical path.  Same bound and result as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t phase, uint64_t limit_ns = 2000000000ull) {
+  if (mbar_test_wait(bar, phase)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (!mbar_test_wait(bar, phase)) {
+    if ((++n & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes % 16 == 0,
 // both addresses 16-byte aligned).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
