@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(192, 1)
       const int qq = (qt_first + it % per_head) * C::BQ + tid;
       const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + qq;
       const bool ok = it < ntiles && qq < p.T;
-      pre_invR = ok ? 1.0f / __ldg(p.rowsum + idx) : 0.f;
+      pre_invR = ok ? __ldg(p.rowsum + idx) : 0.f;  // inverted when stored (no stall here)
       pre_delta = ok ? __ldg(p.delta + idx) : 0.f;
     };
     prefetch(0);
@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(192, 1)
       const int q0 = (qt_first + it % per_head) * C::BQ;
       const int64_t rbase = ((int64_t)b * p.Hq + h) * p.T;
       compute_sync();  // everyone done with the previous tile's invR / delta
-      sInvR[tid] = pre_invR;
+      sInvR[tid] = pre_invR > 0.f ? 1.0f / pre_invR : 0.f;
       sDelta[tid] = pre_delta;
       compute_sync();
       prefetch(it + 1);
@@ -711,14 +711,17 @@ __global__ void __launch_bounds__(448, 1)
       const int qq = (qt_first + it % per_head) * C::BQ + (tid & 63);
       const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + qq;
       const bool ok = it < ntiles && qq < p.T;
-      pre = !ok ? 0.f : (tid < 64 ? 1.0f / __ldg(p.rowsum + idx) : __ldg(p.delta + idx));
+      // raw load only: arithmetic on the loaded value here would stall this
+      // warp for the full global-load latency before the tile's barrier
+      pre = !ok ? 0.f : __ldg((tid < 64 ? p.rowsum : p.delta) + idx);
     };
     prefetch(0);
     for (int it = 0; it < ntiles && !failed; ++it) {
       const int bb = it & 1;
       const int q0 = (qt_first + it % per_head) * C::BQ;
       ew_sync();
-      if (tid < 128) (tid < 64 ? vInvR : vDelta)[bb * 64 + (tid & 63)] = pre;
+      if (tid < 64) vInvR[bb * 64 + tid] = pre > 0.f ? 1.0f / pre : 0.f;
+      else if (tid < 128) vDelta[bb * 64 + (tid & 63)] = pre;
       ew_sync();
       prefetch(it + 1);
       // all 256 threads leave together on a timeout (the chunk below has a named barrier)
