@@ -704,24 +704,29 @@ __global__ void __launch_bounds__(448, 1)
     const int tid = threadIdx.x;  // 0..255
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     const float scale2 = 2.0f * p.scale, c4s = 4.0f * p.scale;
+    // R (threads 0..63) or delta (64..127) of the next tile's query column is
+    // loaded a tile ahead into a register.  The load is unconditional (from a
+    // valid index) and the validity flag is applied when the value is used,
+    // so nothing waits on the load before the tile's barrier.
     float pre = 0.f;
-    auto prefetch = [&](int it) {  // threads 0..63: invR, 64..127: delta
+    bool pre_ok = false;
+    auto prefetch = [&](int it) {
       if (tid >= 128) return;
-      const int h = kvh * G + it / per_head;
-      const int qq = (qt_first + it % per_head) * C::BQ + (tid & 63);
-      const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + qq;
-      const bool ok = it < ntiles && qq < p.T;
-      // raw load only: arithmetic on the loaded value here would stall this
-      // warp for the full global-load latency before the tile's barrier
-      pre = !ok ? 0.f : __ldg((tid < 64 ? p.rowsum : p.delta) + idx);
+      const int itc = it < ntiles ? it : 0;
+      const int h = kvh * G + itc / per_head;
+      const int qq = (qt_first + itc % per_head) * C::BQ + (tid & 63);
+      pre_ok = it < ntiles && qq < p.T;
+      const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + (qq < p.T ? qq : 0);
+      pre = __ldg((tid < 64 ? p.rowsum : p.delta) + idx);
     };
     prefetch(0);
     for (int it = 0; it < ntiles && !failed; ++it) {
       const int bb = it & 1;
       const int q0 = (qt_first + it % per_head) * C::BQ;
-      ew_sync();
-      if (tid < 64) vInvR[bb * 64 + tid] = pre > 0.f ? 1.0f / pre : 0.f;
-      else if (tid < 128) vDelta[bb * 64 + (tid & 63)] = pre;
+      // buffer bb was last read in tile it-2; every thread finished that
+      // before the barrier below of tile it-1, so no barrier is needed here
+      if (tid < 64) vInvR[bb * 64 + tid] = pre_ok ? 1.0f / pre : 0.f;
+      else if (tid < 128) vDelta[bb * 64 + (tid & 63)] = pre_ok ? pre : 0.f;
       ew_sync();
       prefetch(it + 1);
       // all 256 threads leave together on a timeout (the chunk below has a named barrier)
