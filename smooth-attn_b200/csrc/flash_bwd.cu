@@ -416,8 +416,8 @@ struct Bwd128 {
   static constexpr int OFF_Q = OFF_V + KV_TILE;
   static constexpr int OFF_DO = OFF_Q + NS * Q_TILE;
   static constexpr int OFF_DS = OFF_DO + NS * Q_TILE;
-  static constexpr int OFF_VEC = OFF_DS + 2 * DS_TILE;  // invR[2][64], delta[2][64]
-  static constexpr int OFF_BAR = OFF_VEC + 4 * 64 * 4;
+  static constexpr int OFF_VEC = OFF_DS + 2 * DS_TILE;  // [2 buffers][3][64] per-column constants
+  static constexpr int OFF_BAR = OFF_VEC + 2 * 3 * 64 * 4;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static constexpr int THREADS = 448;
 };
@@ -450,54 +450,66 @@ __device__ __forceinline__ bool ew_all(bool v) {
   return out != 0;
 }
 
+// Per query column m the loader stores c4[m] = 1/(4R), cs[m] = scale/R and
+// cd[m] = delta*scale/R, so with t = a + sqrt(a^2+4) = 2 sp and
+// h = 1 + a rsqrt(a^2+4) = 2 sp':
+//   P  = sp^2 / R                      = t*t*c4
+//   dS = (dP - delta)/R * 4 sp sp' s   = (dP*cs - cd) * t*h
+// Both 32-column TMEM loads are issued together (one latency); results are
+// packed and stored 16 columns at a time to keep register use low.
 template <bool BF16, bool EXACT, bool MASK>
 __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, uint8_t* dsrow, int r,
-                                             const float* vInvR, const float* vDelta, float scale2, float c4s, int n,
-                                             int q0, int T, int window) {
+                                             const float* vec, float scale2, int n, int q0, int T, int window) {
   uint32_t sv[32], dv[32];
   tmem_ld32(tS + 32 * w2, sv);
   tmem_ld32(tP + 32 * w2, dv);
   tmem_ld_wait(sv);
   tmem_ld_wait(dv);
-  uint32_t pk[16], dk[16];
 #pragma unroll
-  for (int e = 0; e < 32; e += 4) {
-    const float4 ir = *reinterpret_cast<const float4*>(vInvR + 32 * w2 + e);
-    const float4 de = *reinterpret_cast<const float4*>(vDelta + 32 * w2 + e);
-    const float irs[4] = {ir.x, ir.y, ir.z, ir.w};
-    const float des[4] = {de.x, de.y, de.z, de.w};
-    float pv[4], dsv[4];
+  for (int hf = 0; hf < 2; ++hf) {
+    const int col = 32 * w2 + 16 * hf;
+    uint32_t pk[8], dk[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
-      const float w = fmaf(a, a, 4.0f);
-      const float rs = rsqrt_approx(w);
-      const float sq = EXACT ? sqrtf(w) : w * rs;
-      const float sp = 0.5f * (a + sq);
-      const float spp = 0.5f * fmaf(a, rs, 1.0f);
-      float pp = sp * sp * irs[u];
-      float ds = (__uint_as_float(dv[e + u]) - des[u]) * irs[u] * (c4s * sp * spp);
-      if (MASK) {
-        const int q = q0 + 32 * w2 + e + u;
-        const bool ok = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
-        pp = ok ? pp : 0.f;
-        ds = ok ? ds : 0.f;
+    for (int e = 0; e < 16; e += 4) {
+      const float4 c4v = *reinterpret_cast<const float4*>(vec + col + e);
+      const float4 csv = *reinterpret_cast<const float4*>(vec + 64 + col + e);
+      const float4 cdv = *reinterpret_cast<const float4*>(vec + 128 + col + e);
+      const float c4[4] = {c4v.x, c4v.y, c4v.z, c4v.w};
+      const float cs[4] = {csv.x, csv.y, csv.z, csv.w};
+      const float cd[4] = {cdv.x, cdv.y, cdv.z, cdv.w};
+      float pv[4], dsv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = 16 * hf + e + u;
+        const float a = fmaf(__uint_as_float(sv[idx]), scale2, -1.0f);
+        const float w = fmaf(a, a, 4.0f);
+        const float rs = rsqrt_approx(w);
+        const float t = EXACT ? a + sqrtf(w) : fmaf(w, rs, a);
+        const float hh = fmaf(a, rs, 1.0f);
+        float pp = t * t * c4[u];
+        float ds = fmaf(__uint_as_float(dv[idx]), cs[u], -cd[u]) * (t * hh);
+        if (MASK) {
+          const int q = q0 + col + e + u;
+          const bool ok = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
+          pp = ok ? pp : 0.f;
+          ds = ok ? ds : 0.f;
+        }
+        pv[u] = pp;
+        dsv[u] = ds;
       }
-      pv[u] = pp;
-      dsv[u] = ds;
+      pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
+      pk[e / 2 + 1] = BF16 ? pack2_bf16(pv[2], pv[3]) : pack2_f16(pv[2], pv[3]);
+      dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
+      dk[e / 2 + 1] = BF16 ? pack2_bf16(dsv[2], dsv[3]) : pack2_f16(dsv[2], dsv[3]);
     }
-    pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
-    pk[e / 2 + 1] = BF16 ? pack2_bf16(pv[2], pv[3]) : pack2_f16(pv[2], pv[3]);
-    dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
-    dk[e / 2 + 1] = BF16 ? pack2_bf16(dsv[2], dsv[3]) : pack2_f16(dsv[2], dsv[3]);
-  }
-  // P of query columns [32 w2, 32 w2 + 32) goes over this warpgroup's own,
-  // already-read S^T columns [32 w2, 32 w2 + 16): no cross-warpgroup hazard.
-  tmem_st16(tS + 32 * w2, pk);
+    // P of query columns [32 w2, 32 w2 + 32) goes over this warpgroup's own,
+    // already-read S^T columns [32 w2, 32 w2 + 16): no cross-warpgroup hazard.
+    tmem_st8(tS + 32 * w2 + 8 * hf, pk);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int piece = (w2 * 4 + j) ^ (r & 7);
-    *reinterpret_cast<uint4*>(dsrow + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+    for (int j = 0; j < 2; ++j) {
+      const int piece = (w2 * 4 + hf * 2 + j) ^ (r & 7);
+      *reinterpret_cast<uint4*>(dsrow + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+    }
   }
 }
 
@@ -515,8 +527,7 @@ __global__ void __launch_bounds__(448, 1)
   uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sDO = smem + C::OFF_DO;
   uint8_t* sDS = smem + C::OFF_DS;
-  float* vInvR = reinterpret_cast<float*>(smem + C::OFF_VEC);  // [2][64]
-  float* vDelta = vInvR + 128;                                  // [2][64]
+  float* vVec = reinterpret_cast<float*>(smem + C::OFF_VEC);  // [2][3][64]
   Bwd128Bars* bars = reinterpret_cast<Bwd128Bars*>(smem + C::OFF_BAR);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -703,21 +714,22 @@ __global__ void __launch_bounds__(448, 1)
     const int n = n0 + r;
     const int tid = threadIdx.x;  // 0..255
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
-    const float scale2 = 2.0f * p.scale, c4s = 4.0f * p.scale;
-    // R (threads 0..63) or delta (64..127) of the next tile's query column is
-    // loaded a tile ahead into a register.  The load is unconditional (from a
-    // valid index) and the validity flag is applied when the value is used,
+    const float scale2 = 2.0f * p.scale;
+    // R and delta of the next tile's query column `tid` (threads 0..63) are
+    // loaded a tile ahead into registers.  The loads are unconditional (from a
+    // valid index) and the validity flag is applied when the values are used,
     // so nothing waits on the load before the tile's barrier.
-    float pre = 0.f;
+    float pre_r = 0.f, pre_d = 0.f;
     bool pre_ok = false;
-    auto prefetch = [&](int it) {
-      if (tid >= 128) return;
+    auto prefetch = [&](int it) {  // threads 0..63: R and delta of query column tid
+      if (tid >= 64) return;
       const int itc = it < ntiles ? it : 0;
       const int h = kvh * G + itc / per_head;
-      const int qq = (qt_first + itc % per_head) * C::BQ + (tid & 63);
+      const int qq = (qt_first + itc % per_head) * C::BQ + tid;
       pre_ok = it < ntiles && qq < p.T;
       const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + (qq < p.T ? qq : 0);
-      pre = __ldg((tid < 64 ? p.rowsum : p.delta) + idx);
+      pre_r = __ldg(p.rowsum + idx);
+      pre_d = __ldg(p.delta + idx);
     };
     prefetch(0);
     for (int it = 0; it < ntiles && !failed; ++it) {
@@ -725,8 +737,13 @@ __global__ void __launch_bounds__(448, 1)
       const int q0 = (qt_first + it % per_head) * C::BQ;
       // buffer bb was last read in tile it-2; every thread finished that
       // before the barrier below of tile it-1, so no barrier is needed here
-      if (tid < 64) vInvR[bb * 64 + tid] = pre_ok ? 1.0f / pre : 0.f;
-      else if (tid < 128) vDelta[bb * 64 + (tid & 63)] = pre_ok ? pre : 0.f;
+      if (tid < 64) {
+        const float ir = pre_ok ? 1.0f / pre_r : 0.f;
+        float* vb = vVec + bb * 192;
+        vb[tid] = 0.25f * ir;
+        vb[64 + tid] = p.scale * ir;
+        vb[128 + tid] = pre_d * p.scale * ir;
+      }
       ew_sync();
       prefetch(it + 1);
       // all 256 threads leave together on a timeout (the chunk below has a named barrier)
@@ -740,11 +757,11 @@ __global__ void __launch_bounds__(448, 1)
                              (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
       uint8_t* dsrow = sDS + bb * C::DS_TILE + r * 128;
       if (need_mask)
-        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
-                                        vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
+        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vVec + bb * 192, scale2,
+                                        n, q0, p.T, p.window);
       else
-        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vInvR + bb * 64,
-                                         vDelta + bb * 64, scale2, c4s, n, q0, p.T, p.window);
+        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vVec + bb * 192, scale2,
+                                         n, q0, p.T, p.window);
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
