@@ -543,6 +543,17 @@ __global__ void __launch_bounds__(448, 1)
   }
   const int per_head = qt_last - qt_first + 1;
   const int ntiles = G * per_head;
+  // Tiles run head-major: (head kvh*G + g, query tile qt_first .. qt_last).
+  // Each role walks them with an incremental cursor (no integer division).
+  struct Cursor {
+    int h, qt;
+  };
+  auto advance = [&](Cursor& c) {
+    if (++c.qt > qt_last) {
+      c.qt = qt_first;
+      ++c.h;
+    }
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
@@ -580,11 +591,12 @@ __global__ void __launch_bounds__(448, 1)
         tma_load_4d(sK + c * 128 * 128, &tmk, c * 64, n0, kvh, b, &bars->kv_full);
         tma_load_4d(sV + c * 128 * 128, &tmv, c * 64, n0, kvh, b, &bars->kv_full);
       }
-      for (int it = 0; it < ntiles && !failed; ++it) {
+      Cursor cur{kvh * G, qt_first};
+      for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
         const int st = it % C::NS;
         if (it >= C::NS && !b_wait(&bars->q_empty[st], ((it / C::NS) - 1) & 1, failed)) break;
-        const int h = kvh * G + it / per_head;
-        const int q0 = (qt_first + it % per_head) * C::BQ;
+        const int h = cur.h;
+        const int q0 = cur.qt * C::BQ;
         mbar_arrive_expect_tx(&bars->q_full[st], 2 * C::Q_TILE);
         for (int c = 0; c < 2; ++c) {
           tma_load_4d(sQ + st * C::Q_TILE + c * C::BQ * 128, &tmq, c * 64, q0, h, b, &bars->q_full[st]);
@@ -685,7 +697,8 @@ __global__ void __launch_bounds__(448, 1)
     const int g = warp & 3;
     const int d = 32 * g + lane;  // TMEM lane = head-dim index of dQ^T
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
-    for (int it = 0; it < ntiles && !failed; ++it) {
+    Cursor cur{kvh * G, qt_first};
+    for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
       if (!b_warp_wait(&bars->mm2_done, it & 1, failed)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
@@ -695,8 +708,8 @@ __global__ void __launch_bounds__(448, 1)
       tmem_ld_wait(v1);
       tc_fence_before();
       mbar_arrive(&bars->dq_free);
-      const int h = kvh * G + it / per_head;
-      const int q0 = (qt_first + it % per_head) * C::BQ;
+      const int h = cur.h;
+      const int q0 = cur.qt * C::BQ;
       float* dst = p.dq_acc + (((int64_t)b * p.Hq + h) * p.T + q0) * D + d;
       const int lim = p.T - q0;
 #pragma unroll
@@ -721,20 +734,23 @@ __global__ void __launch_bounds__(448, 1)
     // so nothing waits on the load before the tile's barrier.
     float pre_r = 0.f, pre_d = 0.f;
     bool pre_ok = false;
+    Cursor nxt{kvh * G, qt_first};  // tile the next prefetch loads
     auto prefetch = [&](int it) {  // threads 0..63: R and delta of query column tid
+      const Cursor c = nxt;
+      advance(nxt);
       if (tid >= 64) return;
-      const int itc = it < ntiles ? it : 0;
-      const int h = kvh * G + itc / per_head;
-      const int qq = (qt_first + itc % per_head) * C::BQ + tid;
+      const int h = it < ntiles ? c.h : kvh * G;
+      const int qq = c.qt * C::BQ + tid;
       pre_ok = it < ntiles && qq < p.T;
       const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + (qq < p.T ? qq : 0);
       pre_r = __ldg(p.rowsum + idx);
       pre_d = __ldg(p.delta + idx);
     };
     prefetch(0);
-    for (int it = 0; it < ntiles && !failed; ++it) {
+    Cursor cur{kvh * G, qt_first};
+    for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
       const int bb = it & 1;
-      const int q0 = (qt_first + it % per_head) * C::BQ;
+      const int q0 = cur.qt * C::BQ;
       // buffer bb was last read in tile it-2; every thread finished that
       // before the barrier below of tile it-1, so no barrier is needed here
       if (tid < 64) {
