@@ -55,6 +55,15 @@ __device__ __forceinline__ bool b_wait(uint64_t* bar, uint32_t phase, bool& fail
   return true;
 }
 
+__device__ __forceinline__ bool b_warp_wait_spin(uint64_t* bar, uint32_t phase, bool& failed) {
+  const bool ok = __all_sync(0xffffffffu, !failed && mbar_wait_spin(bar, phase));
+  if (!ok) {
+    if (!failed && (threadIdx.x & 31) == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
+    failed = true;
+  }
+  return ok;
+}
+
 __device__ __forceinline__ bool b_warp_wait(uint64_t* bar, uint32_t phase, bool& failed) {
   const bool ok = __all_sync(0xffffffffu, !failed && mbar_wait(bar, phase));
   if (!ok) {
@@ -699,7 +708,8 @@ __global__ void __launch_bounds__(448, 1)
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     Cursor cur{kvh * G, qt_first};
     for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
-      if (!b_warp_wait(&bars->mm2_done, it & 1, failed)) break;
+      // polling (not suspending): the drain's reaction time gates the next dP^T
+      if (!b_warp_wait_spin(&bars->mm2_done, it & 1, failed)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
       tmem_ld32(tl + 128 + (it & 1) * 64, v0);  // dQ^T(it) sits in dP^T buffer it&1
