@@ -218,6 +218,10 @@ def run_ours(args):
     if args.only == "all" and not args.skip_flash:
         flash = run_flash(args, world, rank, tf_burst, tf_sus, peak_kind)
 
+    extra = None
+    if args.only == "all" and not args.skip_extra:
+        extra = run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind)
+
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline(args.cpu_seconds)
@@ -245,6 +249,8 @@ def run_ours(args):
         }
         if flash is not None:
             line["flash_fwd_bwd"] = flash
+        if extra is not None:
+            line["other_configs"] = extra
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -296,6 +302,86 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
                      "frac_of_burst": round(fwd_flops_loc / (fwd_ms * 1e-3) / 1e12 / tf_burst, 4)},
         "flops_per_step": flops_all,
     }
+
+
+def run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind):
+    """The other BASELINE configs, one object each (parity spot-checks ride along).
+
+    configs[1] sweep over L, configs[1] row-wise fp32, configs[2] causal norm
+    forward + fused backward, configs[4] long-context attention forward.
+    Inputs are generated on the device from seeded generators.
+    """
+    import smooth_attn as sa
+    from oracle import sa_oracle as O
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(777 + rank)
+    out = {}
+
+    def gbs(nbytes, ms):
+        return round(nbytes / (ms * 1e-3) / 1e9, 1)
+
+    # configs[1]: causal norm forward, bf16 [8,16,L,L], L swept
+    sweep = {}
+    for L in (128, 256, 512, 1024, 2048):
+        x = torch.randn(8, 16, L, L, device=dev, generator=g).to(torch.bfloat16)
+        o = torch.empty_like(x)
+        n = max(20, 200 * 128 // L)
+        for _ in range(3):
+            sa.softplus_norm_causal_triton_out(o, x)
+        ms = time_steps(lambda: sa.softplus_norm_causal_triton_out(o, x), n, world) / n
+        b = norm_bytes(8 * 16, L)
+        sweep[str(L)] = {"us": round(ms * 1e3, 2), "GB/s": gbs(b, ms), "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 3),
+                         "inputs_vs_L2": "larger" if x.numel() * 2 > 126e6 else "smaller (L2-resident, warm)"}
+        del x, o
+    out["causal_norm_sweep"] = {"config": "BASELINE configs[1]: bf16 [8,16,L,L] out-buffer path", "per_L": sweep}
+
+    # configs[1] row-wise: fp32 [4,16,2048,2048] viewed [131072, 2048]
+    x = torch.randn(131072, 2048, device=dev, generator=g)
+    o = torch.empty_like(x)
+    for _ in range(3):
+        sa.softplus_norm_triton_out(o, x)
+    ms = time_steps(lambda: sa.softplus_norm_triton_out(o, x), 50, world) / 50
+    b = x.numel() * 8
+    err = float((o[:4].cpu() - torch.from_numpy(O.softplus_norm(x[:4].cpu().numpy()))).abs().max())
+    out["rowwise_fp32"] = {"config": "BASELINE configs[1] row-wise: fp32 [131072, 2048]", "ms": round(ms, 4),
+                           "GB/s": gbs(b, ms), "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 3),
+                           "max_abs_err_vs_oracle": err}
+    del x, o
+
+    # configs[2]: causal norm forward + fused backward, bf16 [4,32,2048,2048]
+    L, M = 2048, 4 * 32
+    x = torch.randn(4, 32, L, L, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(4, 32, L, L, device=dev, generator=g).to(torch.bfloat16)
+
+    def fb():
+        y = sa.softplus_norm_causal(x)
+        torch.autograd.grad(y, x, dy)
+
+    for _ in range(3):
+        fb()
+    ms = time_steps(fb, 20, world) / 20
+    tri = L * (L + 1) // 2
+    b = M * (2 * tri + 2 * L * L) + 4 * M * L + M * (2 * 2 * tri + 2 * L * L) + 4 * M * L
+    out["causal_norm_fwd_bwd"] = {"config": "BASELINE configs[2]: bf16 [4,32,2048,2048] fwd + fused bwd (autograd)",
+                                  "ms": round(ms, 4), "GB/s": gbs(b, ms),
+                                  "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 3), "algorithmic_bytes": b}
+    del x, dy
+
+    # configs[4]: long-context attention forward, bf16 [2,64,32768,128] per GPU
+    B, H, T, D = 2, 64, 32768, 128
+    q, k, v = (torch.randn(B, H, T, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+    for _ in range(2):
+        sa.sp2norm_flash_attention(q, k, v)
+    ms = time_steps(lambda: sa.sp2norm_flash_attention(q, k, v), 3, world) / 3
+    fl = O.flash_flops(B, H, T, D)
+    out["long_context_fwd"] = {"config": "BASELINE configs[4]: bf16 [2,64,32768,128] forward, one block of heads per GPU",
+                               "ms": round(ms, 3), "TFLOP/s_per_gpu": round(fl / (ms * 1e-3) / 1e12, 1),
+                               "TFLOP/s_all": round(world * fl / (ms * 1e-3) / 1e12, 1),
+                               "frac_of_burst": round(fl / (ms * 1e-3) / 1e12 / tf_burst, 3)}
+    del q, k, v
+    torch.cuda.empty_cache()
+    return out
 
 
 CPU_BLOCK_ROWS = 128  # CPU sample unit: a 128-row block of one [2048, 2048] causal matrix
@@ -385,6 +471,7 @@ def main():
     ap.add_argument("--flash-shape", default=",".join(str(FLASH_CFG[k]) for k in "BHTD"),
                     help="B,H,T,D of the attention workload (BASELINE: 4,32,4096,128)")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-extra", action="store_true", help="skip the other BASELINE configs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--traffic-bytes", type=float, default=NORM_TRAFFIC_BYTES,
                     help="ncu dram bytes per launch of the norm kernel, if measured")
