@@ -54,6 +54,8 @@ SA_API const char* sa_last_cuda_error(void);
  * Device-side status of the current device: SA_ERR_TIMEOUT if any kernel of
  * this library gave up a bounded wait (an mbarrier / copy that never
  * completed) since the last reset, else SA_OK.  Synchronises the device.
+ * Otherwise SA_ERR_ARG if sa_paged_decode met a block_table entry outside
+ * [0, num_blocks) since the last reset.
  * reset != 0 clears the recorded status.  (No reference counterpart: the
  * reference's Triton kernels have no bounded waits.)
  */
@@ -168,6 +170,40 @@ SA_API int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, con
                                 const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
                                 const int64_t* dv_strides, float scale, int64_t window_size, int exact_math,
                                 int dtype, void* stream);
+
+/*
+ * Workspace bytes sa_paged_decode needs for this shape (0 when the launch
+ * does not split sequences over several CTAs), or a negative sa_status when
+ * the shape is rejected.  Depends on the current device's SM count.
+ */
+SA_API int64_t sa_paged_decode_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks,
+                                              int64_t block_size, int64_t D, int dtype);
+
+/*
+ * Decode attention (one query token per sequence) over a paged KV cache.
+ *   s_j = (q . k_j) * scale;  y_j = squareplus(2 s_j - 1)^2;
+ *   out = sum_j y_j v_j / (sum_j y_j + 1e-12)   over j < context_lens[b]
+ * q: [B, Hq, 1, D] contiguous; k_cache, v_cache: [num_blocks, Hkv,
+ * block_size, D] contiguous; token j of sequence b is row j % block_size of
+ * page block_table[b, j / block_size]; block_table: int32 [B, max_blocks]
+ * contiguous; context_lens: int32 [B] (clamped to [0, max_blocks *
+ * block_size]).  out: bf16 [B, Hq, D] contiguous.  dtype (q and caches):
+ * SA_BF16 or SA_F16; D in {32, 64, 128, 256}; Hq % Hkv == 0.  Pointers
+ * 16-byte aligned.  workspace: sa_paged_decode_workspace_size() bytes,
+ * 256-byte aligned; its first bytes hold per-(sequence, head) arrival
+ * tickets that must be zero before the first call and that every completed
+ * call leaves zero again, so one zero-filled workspace can be reused by
+ * calls that do not overlap on the GPU.  Page indices outside
+ * [0, num_blocks) are read as page 0 and reported by sa_device_status.
+ *
+ * Replaces: sp2norm_paged_attention / _sp2norm_paged_attention_kernel
+ *             (src/smooth_attn/kernels.py:2776-2829, :2681-2773)
+ */
+SA_API int sa_paged_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
+                           const int32_t* block_table, const int32_t* context_lens, void* workspace,
+                           int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t num_blocks,
+                           int64_t block_size, int64_t max_blocks, int64_t D, float scale, int dtype,
+                           void* stream);
 
 #ifdef __cplusplus
 }

@@ -235,6 +235,42 @@ def sp2norm_flash_attention_bwd(q, k, v, do, scale=None, window_size=0, acc=np.f
     return dq, dk, dv
 
 
+def paged_decode_attention(q, k_cache, v_cache, block_table, context_lens, scale=None, acc=np.float32):
+    """Decode attention over a paged KV cache (kernels.py:2681-2829 and the
+    reference's decode reference, tests/test_paged_attention.py:78-109).
+
+    q: [B, H_q, 1, D]; k_cache, v_cache: [num_blocks, H_kv, block_size, D];
+    block_table: [B, max_blocks] physical page of each logical page;
+    context_lens: [B].  The single query of sequence b sees all of its
+    context_lens[b] tokens (no causal mask).  Returns [B, H_q, D] in ``acc``:
+      y = squareplus(2 s - 1)^2 with s = (q . k) * scale,
+      o = sum(y v) / (sum(y) + 1e-12).
+    """
+    q = _as_f(q, acc)
+    kc = _as_f(k_cache, acc)
+    vc = _as_f(v_cache, acc)
+    B, Hq, _, D = q.shape
+    Hkv, bs = kc.shape[1], kc.shape[2]
+    G = Hq // Hkv
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    out = np.zeros((B, Hq, D), dtype=acc)
+    for b in range(B):
+        n = int(context_lens[b])
+        pages = [int(block_table[b, i]) for i in range((n + bs - 1) // bs)]
+        if not pages:
+            continue
+        k = np.concatenate([kc[pg] for pg in pages], axis=1)[:, :n]  # [Hkv, n, D]
+        v = np.concatenate([vc[pg] for pg in pages], axis=1)[:, :n]
+        for h in range(Hq):
+            s = (k[h // G] @ q[b, h, 0]) * acc(scale)
+            a = acc(2.0) * s - acc(1.0)
+            sp = acc(0.5) * (a + np.sqrt(a * a + acc(4.0)))
+            y = sp * sp
+            out[b, h] = (y @ v[h // G]) / (y.sum() + acc(EPS))
+    return out
+
+
 def flash_flops(B, H, T, D, window_size=0, bwd=False):
     """Algorithmic FLOPs of causal squareplus attention.
 

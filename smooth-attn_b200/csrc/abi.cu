@@ -16,12 +16,16 @@ namespace sa {
 int norm_timeouts(int reset);  // norm.cu
 int flash_timeouts(int reset);      // flash_fwd.cu
 int flash_bwd_timeouts(int reset);  // flash_bwd.cu
+int paged_timeouts(int reset);      // paged.cu
+int paged_bad_pages(int reset);     // paged.cu
 }  // namespace sa
 
 extern "C" int sa_device_status(int reset) {
   if (cudaDeviceSynchronize() != cudaSuccess) return sa_record_cuda_error(cudaGetLastError());
-  const int n = sa::norm_timeouts(reset) + sa::flash_timeouts(reset) + sa::flash_bwd_timeouts(reset);
-  return n ? SA_ERR_TIMEOUT : SA_OK;
+  const int n = sa::norm_timeouts(reset) + sa::flash_timeouts(reset) + sa::flash_bwd_timeouts(reset) +
+                sa::paged_timeouts(reset);
+  const int bad = sa::paged_bad_pages(reset);
+  return n ? SA_ERR_TIMEOUT : bad ? SA_ERR_ARG : SA_OK;
 }
 
 extern "C" int sa_version(void) { return (0 << 16) | 1; }

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import threading
 from dataclasses import dataclass
 
 import torch
@@ -535,7 +536,85 @@ def _not_built(name, ref):
 sp2norm_rope_flash_attention = _not_built("sp2norm_rope_flash_attention", "kernels.py:2373-2430")
 sp2norm_rope_flash_attention_proj = _not_built("sp2norm_rope_flash_attention_proj", "kernels.py:2433-2490")
 sp2norm_fp8_flash_attention = _not_built("sp2norm_fp8_flash_attention", "kernels.py:2630-2673")
-sp2norm_paged_attention = _not_built("sp2norm_paged_attention", "kernels.py:2776-2829")
+
+
+# ---------------------------------------------------------------------------
+# paged-KV decode (kernels.py:2681-2829)
+# ---------------------------------------------------------------------------
+
+PAGED_HEAD_DIMS = (32, 64, 128, 256)
+_paged_ws = {}  # (device index, stream handle) -> zero-ticketed workspace
+_paged_ws_lock = threading.Lock()
+
+
+def _paged_workspace(device, stream_handle, nbytes):
+    """A workspace whose ticket words are zero (every completed call leaves
+    them zero), reused per (device, stream) so calls on one stream never
+    overlap on the GPU."""
+    key = (device.index, stream_handle)
+    with _paged_ws_lock:
+        ws = _paged_ws.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            _paged_ws[key] = ws
+        return ws
+
+
+def sp2norm_paged_attention(q, k_cache, v_cache, block_table, context_lens, *, scale=None, block_size=16):
+    """Paged KV-cache sp2norm attention for autoregressive decode
+    (kernels.py:2776-2829).
+
+    q: [batch, H_q, 1, D]; k_cache, v_cache: [num_blocks, H_kv, block_size, D];
+    block_table: [batch, max_blocks_per_seq] logical-to-physical page map;
+    context_lens: [batch] cached tokens per sequence.  Returns the bf16
+    [batch, H_q, D] output of sum_j y_j v_j / (sum_j y_j + 1e-12) with
+    y_j = squareplus(2 (q . k_j) scale - 1)^2 over every cached token
+    (no causal mask), computed by the sm_100a kernel ``sa_paged_decode``.
+    """
+    assert q.ndim == 4 and q.shape[2] == 1, "Decode: q must be [B, H, 1, D]"
+    B, H_q, _, D = q.shape
+    H_kv = k_cache.shape[1]
+    assert H_q % H_kv == 0
+    assert k_cache.shape[2] == block_size and v_cache.shape[2] == block_size
+    max_blocks_per_seq = block_table.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
+        _validate_cuda_tensor(t, name=name)
+    if q.dtype not in (torch.bfloat16, torch.float16) or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise ValueError(f"paged decode needs bf16 or fp16 q/k_cache/v_cache of one dtype, "
+                         f"got {q.dtype}/{k_cache.dtype}/{v_cache.dtype}")
+    if D not in PAGED_HEAD_DIMS:
+        raise ValueError(f"head dim {D} not supported (supported: {PAGED_HEAD_DIMS})")
+    if k_cache.shape != v_cache.shape or k_cache.shape[3] != D:
+        raise ValueError(f"k_cache {tuple(k_cache.shape)} / v_cache {tuple(v_cache.shape)} do not match D={D}")
+    q = q.contiguous()
+    k_cache = k_cache.contiguous()
+    v_cache = v_cache.contiguous()
+    block_table = block_table.to(device=q.device, dtype=torch.int32).contiguous()
+    context_lens = context_lens.to(device=q.device, dtype=torch.int32).contiguous()
+    out = torch.empty(B, H_q, D, device=q.device, dtype=torch.bfloat16)
+    if out.numel() == 0:
+        return out
+    if max_blocks_per_seq == 0 or k_cache.shape[0] == 0:
+        return out.zero_()
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        nbytes = lib.sa_paged_decode_workspace_size(B, H_q, H_kv, max_blocks_per_seq, block_size, D,
+                                                    _DTYPE_CODE[q.dtype])
+        if nbytes < 0:
+            _lib.check(int(nbytes), "sa_paged_decode_workspace_size")
+        stream = _stream(q)
+        ws = _paged_workspace(q.device, stream.value, nbytes) if nbytes > 0 else None
+        st = lib.sa_paged_decode(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+            block_table.data_ptr(), context_lens.data_ptr(),
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            B, H_q, H_kv, k_cache.shape[0], block_size, max_blocks_per_seq, D, float(scale),
+            _DTYPE_CODE[q.dtype], stream,
+        )
+    _lib.check(st, "sa_paged_decode")
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -10,6 +10,9 @@ in float32 with seeded ``torch.Generator`` inputs:
   * ``softplus_norm_eager``               (kernels.py:1332-1346)
   * ``softplus_norm_causal_eager``        (kernels.py:1349-1365) + torch autograd
   * ``sp2norm_flash_attention_eager``     (kernels.py:2053-2084) + torch autograd
+  * ``reference_decode_attention`` of the reference's paged tests
+    (tests/test_paged_attention.py:78-109) on shuffled paged caches built by
+    its ``_build_paged_kv_cache_shuffled`` (:43-75)
 
 and writes ``golden.npz`` next to this script.  The GPU box never runs this
 script (the reference is not present there); the tests only read the
@@ -105,6 +108,30 @@ def main():
         data[f"{name}/dk"] = k.grad.numpy()
         data[f"{name}/dv"] = v.grad.numpy()
         data[f"{name}/window"] = np.array(W)
+
+    # --- paged-KV decode (reference decode reference of the paged tests) ---
+    sys.path.insert(0, str(REF / "tests"))
+    import test_paged_attention as tpa  # noqa: E402  (the reference's own test helpers)
+
+    paged_cases = [
+        # name, B, Hq, Hkv, T (per sequence), D, block_size
+        ("p_basic", 2, 4, 4, 48, 32, 16),
+        ("p_gqa", 2, 8, 2, 100, 64, 16),
+        ("p_bs8", 1, 4, 4, 37, 128, 8),
+    ]
+    for i, (name, B, Hq, Hkv, T, D, BS) in enumerate(paged_cases):
+        q = randn((B, Hq, 1, D), 8000 + i, torch.bfloat16).to(torch.bfloat16)
+        k = randn((B, Hkv, T, D), 8100 + i, torch.bfloat16).to(torch.bfloat16)
+        v = randn((B, Hkv, T, D), 8200 + i, torch.bfloat16).to(torch.bfloat16)
+        torch.manual_seed(8300 + i)  # the shuffled builder draws a permutation
+        kc, vc, bt, cl = tpa._build_paged_kv_cache_shuffled(k, v, block_size=BS)
+        out = tpa.reference_decode_attention(q, k, v)
+        data[f"{name}/q"] = q.float().numpy()
+        data[f"{name}/k_cache"] = kc.float().numpy()
+        data[f"{name}/v_cache"] = vc.float().numpy()
+        data[f"{name}/block_table"] = bt.numpy()
+        data[f"{name}/context_lens"] = cl.numpy()
+        data[f"{name}/out"] = out.float().numpy()
 
     np.savez_compressed(OUT, **data)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(data)} arrays)")

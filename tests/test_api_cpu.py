@@ -91,7 +91,22 @@ def test_bad_implementation():
 
 def test_not_built_extensions_raise():
     with pytest.raises(NotImplementedError):
-        sa.sp2norm_paged_attention(None)
+        sa.sp2norm_fp8_flash_attention(None)
+
+
+def test_paged_decode_rejects_cpu_tensors():
+    """The decode wrapper keeps the reference's shape asserts
+    (kernels.py:2793-2797) and refuses host tensors (no CPU fallback)."""
+    q = torch.zeros(1, 4, 1, 64, dtype=torch.bfloat16)
+    kc = torch.zeros(4, 4, 16, 64, dtype=torch.bfloat16)
+    bt = torch.zeros(1, 4, dtype=torch.int32)
+    cl = torch.full((1,), 64, dtype=torch.int32)
+    with pytest.raises(AssertionError):
+        sa.sp2norm_paged_attention(q[:, :, 0], kc, kc, bt, cl)
+    with pytest.raises(AssertionError):
+        sa.sp2norm_paged_attention(q, kc, kc, bt, cl, block_size=8)
+    with pytest.raises(ValueError, match="CUDA"):
+        sa.sp2norm_paged_attention(q, kc, kc, bt, cl)
 
 
 def test_eager_functions_match_oracle_cpu():
