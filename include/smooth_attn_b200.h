@@ -172,6 +172,46 @@ SA_API int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, con
                                 int dtype, void* stream);
 
 /*
+ * Rotary position embedding, rotate-half form, rounded to the input type:
+ *   out[..., i] = x1 c - x2 s,  out[..., i + D/2] = x2 c + x1 s
+ * with x1 = x[..., i], x2 = x[..., i + D/2], c = cos[t, i], s = sin[t, i],
+ * each product and the sum rounded separately in fp32.
+ * x: [B, H, T, D] with strides {batch, head, seq, dim} (dim stride 1, others
+ * multiples of 8); out: contiguous [B, H, T, D]; cos_table / sin_table:
+ * contiguous [T, D/2] of cs_dtype (SA_F32, SA_BF16 or SA_F16).  dtype:
+ * SA_BF16 or SA_F16; D a multiple of 16.
+ *
+ * Replaces: the in-register RoPE of _sp2norm_rope_flash_fwd_kernel
+ *             (src/smooth_attn/kernels.py:2147-2159, :2186-2194)
+ */
+SA_API int sa_rope_rotate(const void* x, void* out, const void* cos_table, const void* sin_table, int cs_dtype,
+                          int64_t B, int64_t H, int64_t T, int64_t D, const int64_t* x_strides, int dtype,
+                          void* stream);
+
+/* Workspace bytes of sa_rope_flash_fwd (the rotated Q and K), or < 0. */
+SA_API int64_t sa_rope_flash_fwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D);
+
+/*
+ * RoPE + fused causal squareplus attention forward: q and k are rotated
+ * (as sa_rope_rotate) into `workspace` (>= sa_rope_flash_fwd_workspace_size
+ * bytes, 256-byte aligned), then sa_flash_fwd runs on the rotated tensors;
+ * v, o, rowsum, strides, scale, window_size, exact_math and dtype as in
+ * sa_flash_fwd.  o may have any sa_flash_fwd-legal strides, e.g. those of a
+ * [B, T, Hq, D] buffer so that an output projection is one plain GEMM.
+ *
+ * Replaces: sp2norm_rope_flash_attention / _sp2norm_rope_flash_fwd_kernel
+ *             (src/smooth_attn/kernels.py:2373-2430, :2104-2222) and the
+ *           attention part of sp2norm_rope_flash_attention_proj /
+ *           _sp2norm_rope_flash_proj_fwd_kernel (:2433-2490, :2230-2370)
+ */
+SA_API int sa_rope_flash_fwd(const void* q, const void* k, const void* v, void* o, float* rowsum,
+                             const void* cos_table, const void* sin_table, int cs_dtype, void* workspace,
+                             int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D,
+                             const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                             const int64_t* o_strides, float scale, int64_t window_size, int exact_math,
+                             int dtype, void* stream);
+
+/*
  * Workspace bytes sa_paged_decode needs for this shape (0 when the launch
  * does not split sequences over several CTAs), or a negative sa_status when
  * the shape is rejected.  Depends on the current device's SM count.

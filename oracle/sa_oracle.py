@@ -19,6 +19,12 @@ Reference citations (file:line inside NoSelection/smooth-attn):
                     fused kernel uses; equals autograd of the eager causal norm)
   * flash eager     ``src/smooth_attn/kernels.py:2053-2084``
   * flash bwd       ``src/smooth_attn/kernels.py:1680-1909`` (closed form)
+  * paged decode    ``src/smooth_attn/kernels.py:2681-2829`` and the decode
+                    reference of ``tests/test_paged_attention.py:78-109``
+  * RoPE            ``src/smooth_attn/kernels.py:2093-2101`` (tables),
+                    ``:2147-2159`` (rotation), ``tests/test_rope_proj.py:15-30``
+  * RoPE + W_o      ``src/smooth_attn/kernels.py:2354-2370`` and
+                    ``tests/test_rope_proj.py:118-150``
   * EPS             ``src/smooth_attn/kernels.py:57``
 
 All arithmetic is float32 unless ``acc=np.float64`` is requested, matching the
@@ -269,6 +275,53 @@ def paged_decode_attention(q, k_cache, v_cache, block_table, context_lens, scale
             y = sp * sp
             out[b, h] = (y @ v[h // G]) / (y.sum() + acc(EPS))
     return out
+
+
+def round_bf16(x):
+    """Round float32 values to the nearest bfloat16 (ties to even), returned
+    as float32 (what ``tensor.to(torch.bfloat16)`` does)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).astype(np.uint32)
+    nan = np.isnan(np.asarray(x, dtype=np.float32))
+    out = r.view(np.float32).copy()
+    out[nan] = np.nan
+    return out
+
+
+def rope_tables(dim, seq_len, base=10000.0):
+    """cos / sin tables [T, D/2] (kernels.py:2093-2101), float32."""
+    inv_freq = (1.0 / (np.float32(base) ** (np.arange(0, dim, 2, dtype=np.float32) / np.float32(dim)))).astype(np.float32)
+    t = np.arange(seq_len, dtype=np.float32)
+    freqs = np.outer(t, inv_freq).astype(np.float32)
+    return np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
+
+
+def rope_rotate(x, cos, sin, to_bf16=True):
+    """Rotate-half RoPE (tests/test_rope_proj.py:15-30, kernels.py:2147-2159):
+    [x1 c - x2 s, x2 c + x1 s] in float32 with every product and sum rounded,
+    then rounded to bf16 as the reference does before its QK^T dot."""
+    x = np.asarray(x, dtype=np.float32)
+    T, D = x.shape[-2], x.shape[-1]
+    c = np.asarray(cos, dtype=np.float32)[:T]
+    s = np.asarray(sin, dtype=np.float32)[:T]
+    x1, x2 = x[..., : D // 2], x[..., D // 2:]
+    out = np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1).astype(np.float32)
+    return round_bf16(out) if to_bf16 else out
+
+
+def rope_flash_attention(q, k, v, cos, sin, scale=None, window_size=0):
+    """RoPE on q and k, then squareplus flash attention
+    (sp2norm_rope_flash_attention, kernels.py:2373-2430)."""
+    return sp2norm_flash_attention(rope_rotate(q, cos, sin), rope_rotate(k, cos, sin), v, scale=scale,
+                                   window_size=window_size)
+
+
+def rope_flash_attention_proj(q, k, v, w_o, cos, sin, scale=None, window_size=0):
+    """RoPE attention then the per-head output projection summed over heads
+    (sp2norm_rope_flash_attention_proj, kernels.py:2433-2490): out[b, t] =
+    sum_h bf16(o[b, h, t]) @ w_o[h], accumulated in float32."""
+    o = round_bf16(rope_flash_attention(q, k, v, cos, sin, scale=scale, window_size=window_size))
+    return np.einsum("bhtd,hdm->btm", o, np.asarray(w_o, dtype=np.float32)).astype(np.float32)
 
 
 def flash_flops(B, H, T, D, window_size=0, bwd=False):

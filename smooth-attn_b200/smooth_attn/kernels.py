@@ -533,8 +533,83 @@ def _not_built(name, ref):
     return fn
 
 
-sp2norm_rope_flash_attention = _not_built("sp2norm_rope_flash_attention", "kernels.py:2373-2430")
-sp2norm_rope_flash_attention_proj = _not_built("sp2norm_rope_flash_attention_proj", "kernels.py:2433-2490")
+def _rope_tables(cos, sin, T, D, device):
+    assert cos.shape == (T, D // 2) and sin.shape == (T, D // 2)
+    if cos.dtype not in _DTYPE_CODE or sin.dtype != cos.dtype:
+        cos, sin = cos.float(), sin.float()
+    return cos.to(device).contiguous(), sin.to(device).contiguous()
+
+
+def _rope_flash_fwd(q, k, v, cos, sin, scale, window_size, o=None):
+    """Rotate q/k (sa_rope_flash_fwd) and run the tcgen05 forward; ``o`` may be
+    a strided view to write into.  Returns (o, row_sums)."""
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    _flash_check(q, k, v)
+    q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
+    cos, sin = _rope_tables(cos, sin, T, D, q.device)
+    if o is None:
+        o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    row_sums = torch.empty(B, H_q, T, device=q.device, dtype=torch.float32)
+    if q.numel() == 0:
+        return o, row_sums
+    lib = _lib.load()
+    nbytes = lib.sa_rope_flash_fwd_workspace_size(B, H_q, H_kv, T, D)
+    ws = torch.empty(nbytes, device=q.device, dtype=torch.uint8)
+    with torch.cuda.device(q.device):
+        st = lib.sa_rope_flash_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
+            cos.data_ptr(), sin.data_ptr(), _DTYPE_CODE[cos.dtype], ws.data_ptr(), nbytes,
+            B, H_q, H_kv, T, D, _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o),
+            float(scale), int(window_size), 0, _DTYPE_CODE[q.dtype], _stream(q),
+        )
+    _lib.check(st, "sa_rope_flash_fwd")
+    return o, row_sums
+
+
+def sp2norm_rope_flash_attention(q, k, v, cos, sin, *, scale=None, window_size=0):
+    """Fused RoPE + sp2norm flash attention forward (kernels.py:2373-2430).
+
+    q: [B, H_q, T, D], k/v: [B, H_kv, T, D] un-rotated bf16 (or fp16);
+    cos/sin: [T, D/2] tables from ``precompute_rope_cos_sin``.  q and k are
+    rotated (rotate-half form, rounded to 16 bits) by one memory-bound pass,
+    then the tcgen05 forward runs causal (optionally windowed) squareplus
+    attention.  Returns o [B, H_q, T, D] in q's dtype.
+    """
+    assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    assert H_q % H_kv == 0
+    assert D % 2 == 0
+    assert cos.shape == (T, D // 2) and sin.shape == (T, D // 2)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    return _rope_flash_fwd(q, k, v, cos, sin, scale, window_size)[0]
+
+
+def sp2norm_rope_flash_attention_proj(q, k, v, w_o, cos, sin, *, scale=None, window_size=0):
+    """Fused RoPE + sp2norm flash attention + output projection
+    (kernels.py:2433-2490).
+
+    w_o: [H_q, D, D_model].  The attention writes its output straight into a
+    [B, T, H_q, D] buffer, so the projection summed over heads is one plain
+    GEMM [B*T, H_q*D] @ [H_q*D, D_model] with fp32 accumulation (the
+    reference accumulates heads with bf16 atomics).  Returns [B, T, D_model]
+    bf16.
+    """
+    assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    assert H_q % H_kv == 0
+    assert D % 2 == 0
+    assert w_o.shape[0] == H_q and w_o.shape[1] == D
+    D_model = w_o.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o_bthd = torch.empty(B, T, H_q, D, device=q.device, dtype=q.dtype)
+    _rope_flash_fwd(q, k, v, cos, sin, scale, window_size, o=o_bthd.permute(0, 2, 1, 3))
+    w = w_o.to(device=q.device, dtype=q.dtype).reshape(H_q * D, D_model)
+    return torch.matmul(o_bthd.view(B * T, H_q * D), w).view(B, T, D_model).to(torch.bfloat16)
 sp2norm_fp8_flash_attention = _not_built("sp2norm_fp8_flash_attention", "kernels.py:2630-2673")
 
 

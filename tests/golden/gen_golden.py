@@ -13,6 +13,10 @@ in float32 with seeded ``torch.Generator`` inputs:
   * ``reference_decode_attention`` of the reference's paged tests
     (tests/test_paged_attention.py:78-109) on shuffled paged caches built by
     its ``_build_paged_kv_cache_shuffled`` (:43-75)
+  * ``precompute_rope_cos_sin`` (kernels.py:2093-2101) with the RoPE tests'
+    ``apply_rope_eager`` (tests/test_rope_proj.py:15-30) followed by
+    ``sp2norm_flash_attention_eager``, and the per-head projection sum of
+    tests/test_rope_proj.py:134-138
 
 and writes ``golden.npz`` next to this script.  The GPU box never runs this
 script (the reference is not present there); the tests only read the
@@ -132,6 +136,44 @@ def main():
         data[f"{name}/block_table"] = bt.numpy()
         data[f"{name}/context_lens"] = cl.numpy()
         data[f"{name}/out"] = out.float().numpy()
+
+    # --- RoPE attention and RoPE attention + output projection -------------
+    import test_rope_proj as trp  # noqa: E402  (the reference's own test helpers)
+
+    rope_cases = [
+        # name, B, Hq, Hkv, T, D, window, D_model (0 = no projection)
+        ("rope_mha", 1, 2, 2, 64, 32, 0, 0),
+        ("rope_gqa_win", 2, 4, 2, 48, 64, 16, 0),
+        ("rope_proj", 2, 4, 4, 40, 32, 0, 96),
+    ]
+    for i, (name, B, Hq, Hkv, T, D, W, DM) in enumerate(rope_cases):
+        q = randn((B, Hq, T, D), 9000 + i, torch.bfloat16).to(torch.bfloat16)
+        k = randn((B, Hkv, T, D), 9100 + i, torch.bfloat16).to(torch.bfloat16)
+        v = randn((B, Hkv, T, D), 9200 + i, torch.bfloat16).to(torch.bfloat16)
+        cos, sin = ref.precompute_rope_cos_sin(D, T, device="cpu", dtype=torch.float32)
+        q_rot = trp.apply_rope_eager(q.float(), cos, sin).to(torch.bfloat16)
+        k_rot = trp.apply_rope_eager(k.float(), cos, sin).to(torch.bfloat16)
+        # fp32 eager attention on the (bf16-valued) rotated tensors pins the
+        # oracle; the projection below follows the test, which projects the
+        # bf16 eager output.
+        o = ref.sp2norm_flash_attention_eager(q_rot.float(), k_rot.float(), v.float(), window_size=W)
+        o_bf16 = ref.sp2norm_flash_attention_eager(q_rot, k_rot, v, window_size=W)
+        data[f"{name}/q"] = q.float().numpy()
+        data[f"{name}/k"] = k.float().numpy()
+        data[f"{name}/v"] = v.float().numpy()
+        data[f"{name}/cos"] = cos.numpy()
+        data[f"{name}/sin"] = sin.numpy()
+        data[f"{name}/q_rot"] = q_rot.float().numpy()
+        data[f"{name}/k_rot"] = k_rot.float().numpy()
+        data[f"{name}/o"] = o.float().numpy()
+        data[f"{name}/window"] = np.array(W)
+        if DM:
+            w_o = randn((Hq, D, DM), 9300 + i, torch.bfloat16).to(torch.bfloat16) * 0.02
+            proj = torch.zeros(B, T, DM, dtype=torch.float32)
+            for h in range(Hq):  # tests/test_rope_proj.py:134-138
+                proj += torch.matmul(o_bf16[:, h].float(), w_o[h].float())
+            data[f"{name}/w_o"] = w_o.float().numpy()
+            data[f"{name}/proj"] = proj.numpy()
 
     np.savez_compressed(OUT, **data)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(data)} arrays)")
