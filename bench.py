@@ -308,7 +308,10 @@ def run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind):
     """The other BASELINE configs, one object each (parity spot-checks ride along).
 
     configs[1] sweep over L, configs[1] row-wise fp32, configs[2] causal norm
-    forward + fused backward, configs[4] long-context attention forward.
+    forward + fused backward, configs[4] long-context attention forward, plus
+    the two forward-only extensions: paged-KV decode at the reference's
+    decode benchmark shapes (tests/test_paged_long_context.py:115-137) and
+    RoPE attention at its RoPE benchmark shapes (tests/test_rope_proj.py:162-163).
     Inputs are generated on the device from seeded generators.
     """
     import smooth_attn as sa
@@ -380,6 +383,54 @@ def run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind):
                                "TFLOP/s_all": round(world * fl / (ms * 1e-3) / 1e12, 1),
                                "frac_of_burst": round(fl / (ms * 1e-3) / 1e12 / tf_burst, 3)}
     del q, k, v
+    torch.cuda.empty_cache()
+
+    # paged-KV decode: GB/s of K+V bytes read, one call per step through the
+    # public API (host wrapper included), back to back
+    dec = {}
+    for B, Hq, Hkv, T, D in ((1, 32, 8, 8192, 128), (1, 32, 8, 32768, 128), (8, 32, 8, 8192, 128),
+                             (32, 32, 8, 1024, 128), (1, 12, 12, 32768, 64), (8, 32, 32, 8192, 128)):
+        BS = 16
+        nb = B * T // BS
+        q = torch.randn(B, Hq, 1, D, device=dev, generator=g).to(torch.bfloat16)
+        kc = torch.randn(nb, Hkv, BS, D, device=dev, generator=g).to(torch.bfloat16)
+        vc = torch.randn(nb, Hkv, BS, D, device=dev, generator=g).to(torch.bfloat16)
+        bt = torch.randperm(nb, device=dev, generator=g).to(torch.int32).view(B, -1)
+        cl = torch.full((B,), T, dtype=torch.int32, device=dev)
+        f = lambda: sa.sp2norm_paged_attention(q, kc, vc, bt, cl, block_size=BS)
+        for _ in range(3):
+            f()
+        n = 50
+        ms = time_steps(f, n, world) / n
+        b = B * T * Hkv * D * 4
+        key = f"B={B} H={Hq}/{Hkv} T={T} D={D}"
+        dec[key] = {"us": round(ms * 1e3, 1), "GB/s": gbs(b, ms), "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 3),
+                    "kv_bytes": b, "inputs_vs_L2": "larger" if b > 126e6 else "smaller (L2-resident, warm)"}
+        if B == 1 and T == 8192:
+            o = f()
+            ref = O.paged_decode_attention(q.float().cpu().numpy(), kc.float().cpu().numpy(),
+                                           vc.float().cpu().numpy(), bt.cpu().numpy(), cl.cpu().numpy())
+            dec[key]["max_abs_err_vs_oracle"] = float(np.abs(o.float().cpu().numpy() - ref).max())
+        del q, kc, vc, bt, cl
+    out["paged_decode"] = {"config": "paged KV decode, bf16, block_size 16, shuffled pages, public API per call",
+                           "per_shape": dec}
+    torch.cuda.empty_cache()
+
+    # RoPE attention forward (rotation pass + tcgen05 forward), TFLOP/s of the attention
+    rope = {}
+    for B, H, T, D in ((2, 32, 1024, 128), (4, 12, 512, 64), (2, 32, 8192, 128)):
+        q, k, v = (torch.randn(B, H, T, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+        cos, sin = sa.precompute_rope_cos_sin(D, T, device=dev)
+        f = lambda: sa.sp2norm_rope_flash_attention(q, k, v, cos, sin)
+        for _ in range(3):
+            f()
+        n = 20
+        ms = time_steps(f, n, world) / n
+        fl = O.flash_flops(B, H, T, D)
+        rope[f"B={B} H={H} T={T} D={D}"] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1)}
+        del q, k, v
+    out["rope_flash_fwd"] = {"config": "RoPE + causal squareplus attention forward, bf16, public API per call",
+                             "per_shape": rope}
     torch.cuda.empty_cache()
     return out
 
