@@ -212,6 +212,35 @@ SA_API int sa_rope_flash_fwd(const void* q, const void* k, const void* v, void* 
                              int dtype, void* stream);
 
 /*
+ * Per-tensor FP8 (E4M3) quantization of q, k and v (nq / nk / nv elements,
+ * contiguous, multiples of 8, dtype SA_F32 / SA_F16 / SA_BF16):
+ *   scale_t = max(max|x_t| / 448, 1e-12);  x8 = e4m3(clamp(x / scale_t, +-448))
+ * q8, k8: E4M3 bytes; vq: bf16 holding the E4M3-rounded v / scale_v exactly;
+ * scales: device float[3] {q, k, v}; workspace: 12 bytes of device scratch.
+ * Two launches, no host synchronisation.
+ *
+ * Replaces: _quantize_to_fp8 (src/smooth_attn/kernels.py:2592-2601)
+ */
+SA_API int sa_fp8_quantize(const void* q, const void* k, const void* v, int64_t nq, int64_t nk, int64_t nv,
+                           int dtype, void* q8, void* k8, void* vq, float* scales, void* workspace, void* stream);
+
+/*
+ * FP8 causal squareplus attention forward: QK^T on E4M3 tensor cores
+ * (tcgen05 kind::f8f6f4), scores scaled by q_scale * k_scale * scale,
+ * squareplus in fp32, P (bf16) . vq on bf16 tensor cores, times v_scale.
+ * q8, k8: E4M3 [B, Hq|Hkv, T, D] (strides multiples of 16 elements);
+ * vq: bf16 [B, Hkv, T, D]; o: bf16; rowsum as sa_flash_fwd; scales: the
+ * device float[3] written by sa_fp8_quantize.  D in {32, 64, 128}.
+ *
+ * Replaces: _sp2norm_fp8_flash_fwd / _sp2norm_fp8_flash_fwd_kernel
+ *             (src/smooth_attn/kernels.py:2604-2627, :2498-2589)
+ */
+SA_API int sa_fp8_flash_fwd(const void* q8, const void* k8, const void* vq, void* o, float* rowsum,
+                            const float* scales, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D,
+                            const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                            const int64_t* o_strides, float scale, int64_t window_size, void* stream);
+
+/*
  * Workspace bytes sa_paged_decode needs for this shape (0 when the launch
  * does not split sequences over several CTAs), or a negative sa_status when
  * the shape is rejected.  Depends on the current device's SM count.

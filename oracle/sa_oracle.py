@@ -25,6 +25,8 @@ Reference citations (file:line inside NoSelection/smooth-attn):
                     ``:2147-2159`` (rotation), ``tests/test_rope_proj.py:15-30``
   * RoPE + W_o      ``src/smooth_attn/kernels.py:2354-2370`` and
                     ``tests/test_rope_proj.py:118-150``
+  * FP8 attention   ``src/smooth_attn/kernels.py:2498-2673`` (quantization
+                    ``:2592-2601``)
   * EPS             ``src/smooth_attn/kernels.py:57``
 
 All arithmetic is float32 unless ``acc=np.float64`` is requested, matching the
@@ -322,6 +324,53 @@ def rope_flash_attention_proj(q, k, v, w_o, cos, sin, scale=None, window_size=0)
     sum_h bf16(o[b, h, t]) @ w_o[h], accumulated in float32."""
     o = round_bf16(rope_flash_attention(q, k, v, cos, sin, scale=scale, window_size=window_size))
     return np.einsum("bhtd,hdm->btm", o, np.asarray(w_o, dtype=np.float32)).astype(np.float32)
+
+
+E4M3_MAX = 448.0  # kernels.py:2596
+
+
+def round_e4m3(x):
+    """Round float32 values (|x| <= 448) to the nearest E4M3 value, ties to
+    even (3 mantissa bits, exponent bias 7, subnormal quantum 2^-9)."""
+    x = np.asarray(x, dtype=np.float64)
+    ax = np.abs(x)
+    e = np.floor(np.log2(np.maximum(ax, 2.0 ** -9)))
+    e = np.maximum(e, -6.0)  # below 2^-6 the spacing stays 2^-9
+    q = 2.0 ** (e - 3)
+    return (np.round(x / q) * q).astype(np.float32)
+
+
+def quantize_fp8(x):
+    """Per-tensor E4M3 quantization (kernels.py:2592-2601):
+    scale = max(amax / 448, 1e-12) in float32, x8 = e4m3(clamp(x / scale)).
+    Returns (x8 as float32 values, scale)."""
+    x = np.asarray(x, dtype=np.float32)
+    amax = np.float32(np.abs(x).max()) if x.size else np.float32(0)
+    scale = np.maximum(np.float32(amax / np.float32(E4M3_MAX)), np.float32(1e-12)).astype(np.float32)
+    xs = np.clip((x / scale).astype(np.float32), -E4M3_MAX, E4M3_MAX)
+    return round_e4m3(xs), float(scale)
+
+
+def fp8_flash_attention(q, k, v, scale=None, window_size=0):
+    """FP8 squareplus attention forward (kernels.py:2498-2589, :2630-2673):
+    scores = (q8 . k8) * (q_scale k_scale scale); y in float32; P = bf16(y);
+    o = (P v8) v_scale / (sum y + EPS)."""
+    q8, qs = quantize_fp8(q)
+    k8, ks = quantize_fp8(k)
+    v8, vs = quantize_fp8(v)
+    T, D = q8.shape[-2], q8.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    sscale = np.float32(qs * ks * scale)  # the reference forms the product in double
+    k8 = _expand_kv(k8, q8.shape[1])
+    v8 = _expand_kv(v8, q8.shape[1])
+    s = np.matmul(q8, np.swapaxes(k8, -1, -2)).astype(np.float32) * sscale
+    a = s + s - np.float32(1.0)
+    sp = np.float32(0.5) * (a + np.sqrt(a * a + np.float32(4.0)))
+    y = np.where(_flash_mask(T, window_size), sp * sp, np.float32(0.0)).astype(np.float32)
+    r = y.sum(axis=-1, keepdims=True) + np.float32(EPS)
+    o = np.matmul(round_bf16(y), v8).astype(np.float32) * np.float32(vs)
+    return o / r
 
 
 def flash_flops(B, H, T, D, window_size=0, bwd=False):

@@ -41,7 +41,7 @@ using namespace sm100;
 static __device__ unsigned g_flash_bwd_timeouts;
 
 bool make_map_4d(CUtensorMap* map, const void* base, bool bf16, int64_t B, int64_t H, int64_t T, int64_t D,
-                 const int64_t* strides, int chunk, int rows);
+                 const int64_t* strides, int chunk, int rows, bool u8 = false);
 
 namespace {
 

@@ -37,20 +37,30 @@ using namespace sm100;
 
 __device__ unsigned g_flash_timeouts;
 
-template <int D>
+// QK8: Q and K are E4M3 bytes (QK^T on kind::f8f6f4), V and P 16-bit.
+template <int D, bool QK8 = false>
 struct FwdCfg {
   static constexpr int BM = 128, BN = 128;  // rows per Q tile, rows per KV tile
-  static constexpr int CHUNK = D >= 64 ? 64 : D;  // elements per swizzled smem row
+  static constexpr int CHUNK = D >= 64 ? 64 : D;  // V: elements per swizzled smem row
   static constexpr int NCHUNK = D / CHUNK;
-  static constexpr int ROWB = CHUNK * 2;  // bytes per smem row
+  static constexpr int ROWB = CHUNK * 2;  // V: bytes per smem row
   static constexpr uint32_t SWZ = ROWB == 128 ? SW_128B : SW_64B;
   static constexpr int SBO = 8 * ROWB;  // stride between 8-row groups
-  static constexpr int TILE = 128 * D * 2;  // one Q, K or V tile
+  static constexpr int TILE = 128 * D * 2;  // one V tile (and one 16-bit Q or K tile)
+  // Q / K operand tiles: element bytes, swizzled row bytes, elements per row
+  static constexpr int EQ = QK8 ? 1 : 2;
+  static constexpr int QK_ROWB = D * EQ >= 128 ? 128 : D * EQ;
+  static constexpr int QK_CHUNK = QK_ROWB / EQ;
+  static constexpr int QK_NCHUNK = D / QK_CHUNK;
+  static constexpr uint32_t QK_SWZ = QK_ROWB == 128 ? SW_128B : QK_ROWB == 64 ? SW_64B : SW_32B;
+  static constexpr int QK_SBO = 8 * QK_ROWB;
+  static constexpr int QK_TILE = 128 * D * EQ;
+  static constexpr int KSTEP = 32 / EQ;  // MMA K per instruction (32 bytes of K)
   static constexpr int NK = D == 128 ? 2 : (D == 64 ? 3 : 4);  // K ring
   static constexpr int NV = NK;                                  // V ring
   static constexpr int OFF_Q = 0;  // Q tile A, Q tile B
-  static constexpr int OFF_K = OFF_Q + 2 * TILE;
-  static constexpr int OFF_V = OFF_K + NK * TILE;
+  static constexpr int OFF_K = OFF_Q + 2 * QK_TILE;
+  static constexpr int OFF_V = OFF_K + NK * QK_TILE;
   static constexpr int OFF_BAR = OFF_V + NV * TILE;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;  // + barriers + alignment slack
   static constexpr int TMEM_COLS = 512;            // S_A @0, S_B @128, O_A @256, O_B @256+D
@@ -62,7 +72,8 @@ struct FwdParams {
   float* rowsum;
   int64_t so_b, so_h, so_s;
   int B, Hq, Hkv, T, npairs, window;
-  float scale2;  // 2 * scale
+  float scale2;         // 2 * scale
+  const float* dscale;  // QK8: device {q_scale, k_scale, v_scale}; scores also scale by q_scale * k_scale
 };
 
 struct Bars {
@@ -160,11 +171,12 @@ __device__ __forceinline__ float squareplus_row(uint32_t tS, float scale2, int k
   return sum;
 }
 
-template <int D, bool BF16, bool EXACT>
+template <int D, bool BF16, bool EXACT, bool QK8 = false>
 __global__ void __launch_bounds__(320, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, FwdParams p) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, QK8>;
+  static_assert(!QK8 || BF16, "the FP8 forward keeps V and P in bf16");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + C::OFF_Q;
@@ -218,17 +230,19 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      mbar_arrive_expect_tx(&bars->q_full, 2 * C::TILE);
+      mbar_arrive_expect_tx(&bars->q_full, 2 * C::QK_TILE);
       for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_4d(sQ + t * C::TILE + c * 128 * C::ROWB, &tmq, c * C::CHUNK, qbase + t * C::BM, h, b, &bars->q_full);
+        for (int c = 0; c < C::QK_NCHUNK; ++c)
+          tma_load_4d(sQ + t * C::QK_TILE + c * 128 * C::QK_ROWB, &tmq, c * C::QK_CHUNK, qbase + t * C::BM, h, b,
+                      &bars->q_full);
       for (int i = 0; i < j1 - j0 && !failed; ++i) {
         const int kv0 = (j0 + i) * C::BN;
         const int ks = i % C::NK, vs = i % C::NV;
         if (i >= C::NK && !wait_or_flag(&bars->k_empty[ks], ((i / C::NK) - 1) & 1, failed)) break;
-        mbar_arrive_expect_tx(&bars->k_full[ks], C::TILE);
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_4d(sK + ks * C::TILE + c * 128 * C::ROWB, &tmk, c * C::CHUNK, kv0, kvh, b, &bars->k_full[ks]);
+        mbar_arrive_expect_tx(&bars->k_full[ks], C::QK_TILE);
+        for (int c = 0; c < C::QK_NCHUNK; ++c)
+          tma_load_4d(sK + ks * C::QK_TILE + c * 128 * C::QK_ROWB, &tmk, c * C::QK_CHUNK, kv0, kvh, b,
+                      &bars->k_full[ks]);
         if (i >= C::NV && !wait_or_flag(&bars->v_empty[vs], ((i / C::NV) - 1) & 1, failed)) break;
         mbar_arrive_expect_tx(&bars->v_full[vs], C::TILE);
         for (int c = 0; c < C::NCHUNK; ++c)
@@ -238,21 +252,25 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      constexpr uint32_t idesc_s = idesc_f16(128, C::BN, BF16 ? 1 : 0, 0, 0);
+      // kind::f8f6f4 uses the same descriptor fields; format code 0 is E4M3
+      constexpr uint32_t idesc_s = idesc_f16(128, C::BN, (BF16 && !QK8) ? 1 : 0, 0, 0);
       constexpr uint32_t idesc_o = idesc_f16(128, D, BF16 ? 1 : 0, 0, 1);
       const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
       const int jlo[2] = {ja0, jb0}, jhi[2] = {ja1, jb1};
       int s_cnt[2] = {0, 0}, pv_cnt[2] = {0, 0};
       // descriptors are built once and advanced with plain adds in the MMA loops
-      const uint64_t dQ0 = smem_desc(aQ, 16, C::SBO, C::SWZ), dK0 = smem_desc(aK, 16, C::SBO, C::SWZ);
+      const uint64_t dQ0 = smem_desc(aQ, 16, C::QK_SBO, C::QK_SWZ), dK0 = smem_desc(aK, 16, C::QK_SBO, C::QK_SWZ);
       const uint64_t dV0 = smem_desc(aV, 128 * C::ROWB, C::SBO, C::SWZ);
       auto issue_s = [&](int t, int i) {
         const int ks = i % C::NK;
-        const uint64_t dq0 = desc_add(dQ0, t * C::TILE), dk0 = desc_add(dK0, ks * C::TILE);
+        const uint64_t dq0 = desc_add(dQ0, t * C::QK_TILE), dk0 = desc_add(dK0, ks * C::QK_TILE);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = ((kk * 16) / C::CHUNK) * 128 * C::ROWB + ((kk * 16) % C::CHUNK) * 2;
-          mma_ss(tbase + t * 128, desc_add(dq0, off), desc_add(dk0, off), idesc_s, kk > 0);
+        for (int kk = 0; kk < D / C::KSTEP; ++kk) {
+          const uint32_t off = ((kk * C::KSTEP) / C::QK_CHUNK) * 128 * C::QK_ROWB + ((kk * C::KSTEP) % C::QK_CHUNK) * C::EQ;
+          if constexpr (QK8)
+            mma_ss_f8(tbase + t * 128, desc_add(dq0, off), desc_add(dk0, off), idesc_s, kk > 0);
+          else
+            mma_ss(tbase + t * 128, desc_add(dq0, off), desc_add(dk0, off), idesc_s, kk > 0);
         }
         mma_commit(&bars->s_full[t]);
         ++s_cnt[t];
@@ -329,6 +347,13 @@ __global__ void __launch_bounds__(320, 1)
     kv_range(q0, p.T, p.window, jl, jh);
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     const uint32_t tS = tl + t * 128;
+    float scale2 = p.scale2, vscale = 1.0f;
+    if constexpr (QK8) {
+      // reference: scores * (q_scale * k_scale * attn_scale), the product
+      // formed in double on the host and rounded to fp32 once
+      scale2 = 2.0f * (float)((double)__ldg(p.dscale) * (double)__ldg(p.dscale + 1) * (double)(0.5f * p.scale2));
+      vscale = __ldg(p.dscale + 2);
+    }
     float rsum = 4e-12f;  // 4 * EPS (y is carried as 4y)
     for (int j = jl, it = 0; j < jh; ++j, ++it) {
       if (!warp_wait_or_flag(&bars->s_full[t], it & 1, failed)) break;
@@ -337,16 +362,16 @@ __global__ void __launch_bounds__(320, 1)
       const bool need_mask = (k0 + C::BN - 1 > q0) || (k0 + C::BN > p.T) ||
                              (p.window > 0 && q0 + C::BM - 1 - k0 >= p.window);
       if (need_mask)
-        rsum += squareplus_row<BF16, EXACT, true>(tS, p.scale2, k0, q, p.T, p.window);
+        rsum += squareplus_row<BF16, EXACT, true>(tS, scale2, k0, q, p.T, p.window);
       else
-        rsum += squareplus_row<BF16, EXACT, false>(tS, p.scale2, 0, 0, 0, 0);
+        rsum += squareplus_row<BF16, EXACT, false>(tS, scale2, 0, 0, 0, 0);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->p_full[t]);
     }
     if (warp_wait_or_flag(&bars->o_full[t], 0, failed) && jh > jl) {
       tc_fence_after();
-      const float inv = 1.0f / rsum;
+      const float inv = vscale / rsum;
       const bool live = q < p.T;
       uint8_t* orow = static_cast<uint8_t*>(p.o) + 2 * ((int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)q * p.so_s);
 #pragma unroll 1
@@ -395,32 +420,37 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// 4-D map over a [B, H, T, D] tensor (element strides), box {chunk, rows, 1, 1}.
+// 4-D map over a [B, H, T, D] tensor (element strides), box {chunk, rows, 1, 1};
+// u8 selects 1-byte elements (E4M3 operands).
 bool make_map_4d(CUtensorMap* map, const void* base, bool bf16, int64_t B, int64_t H, int64_t T, int64_t D,
-                 const int64_t* strides, int chunk, int rows) {
+                 const int64_t* strides, int chunk, int rows, bool u8 = false) {
   auto enc = get_encode();
   if (!enc) return false;
+  const int es = u8 ? 1 : 2;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
-  cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[0] * 2};
+  cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * es, (cuuint64_t)strides[1] * es, (cuuint64_t)strides[0] * es};
   cuuint32_t box[4] = {(cuuint32_t)chunk, (cuuint32_t)rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapSwizzle swz = chunk * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                 : chunk * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                   : CU_TENSOR_MAP_SWIZZLE_32B;
-  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+  const CUtensorMapSwizzle swz = chunk * es == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : chunk * es == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                    : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUtensorMapDataType dt = u8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 4,
                    const_cast<void*>(base), dims, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-template <int D, bool BF16, bool EXACT>
+template <int D, bool BF16, bool EXACT, bool QK8 = false>
 static int launch_fwd(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B, int64_t Hq,
                       int64_t Hkv, int64_t T, const int64_t* qs, const int64_t* ks, const int64_t* vs,
-                      const int64_t* os, float scale, int64_t window, cudaStream_t st) {
-  using C = FwdCfg<D>;
+                      const int64_t* os, float scale, int64_t window, cudaStream_t st,
+                      const float* dscale = nullptr) {
+  using C = FwdCfg<D, QK8>;
   CUtensorMap mq, mk, mv;
-  if (!make_map_4d(&mq, q, BF16, B, Hq, T, D, qs, C::CHUNK, C::BM) ||
-      !make_map_4d(&mk, k, BF16, B, Hkv, T, D, ks, C::CHUNK, C::BN) ||
+  if (!make_map_4d(&mq, q, BF16, B, Hq, T, D, qs, C::QK_CHUNK, C::BM, QK8) ||
+      !make_map_4d(&mk, k, BF16, B, Hkv, T, D, ks, C::QK_CHUNK, C::BN, QK8) ||
       !make_map_4d(&mv, v, BF16, B, Hkv, T, D, vs, C::CHUNK, C::BN))
     return SA_ERR_ALIGN;
   FwdParams p;
@@ -436,7 +466,8 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, floa
   p.npairs = (int)((T + 2 * C::BM - 1) / (2 * C::BM));
   p.window = (int)window;
   p.scale2 = 2.0f * scale;
-  auto kern = flash_fwd_kernel<D, BF16, EXACT>;
+  p.dscale = dscale;
+  auto kern = flash_fwd_kernel<D, BF16, EXACT, QK8>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   dim3 grid(p.npairs, (unsigned)(B * Hq));
   kern<<<grid, C::THREADS, C::SMEM, st>>>(mq, mk, mv, p);
@@ -502,6 +533,39 @@ extern "C" int sa_flash_fwd(const void* q, const void* k, const void* v, void* o
   }
 #undef SA_FWD_D
 #undef SA_FWD_CASE
+  if (rc != SA_OK) return rc;
+  return sa_record_cuda_error(cudaGetLastError());
+}
+
+extern "C" int sa_fp8_flash_fwd(const void* q8, const void* k8, const void* vq, void* o, float* rowsum,
+                                const float* scales, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D,
+                                const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                                const int64_t* o_strides, float scale, int64_t window_size, void* stream) {
+  if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
+  if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Hq % Hkv != 0 || window_size < 0) return SA_ERR_ARG;
+  if (B == 0 || T == 0) return SA_OK;
+  if (T > (1ll << 30) || B * Hq > 65535) return SA_ERR_UNSUPPORTED;
+  if (!q8 || !k8 || !vq || !o || !rowsum || !scales) return SA_ERR_ARG;
+  auto bytes_ok = [](const int64_t* s) {  // 1-byte elements: TMA strides in 16-byte units
+    return s != nullptr && s[3] == 1 && s[0] % 16 == 0 && s[1] % 16 == 0 && s[2] % 16 == 0 && s[0] >= 0 &&
+           s[1] >= 0 && s[2] > 0;
+  };
+  if (!bytes_ok(q_strides) || !bytes_ok(k_strides) || !strides_ok(v_strides) || !strides_ok(o_strides))
+    return SA_ERR_ALIGN;
+  if (!ptr16(q8) || !ptr16(k8) || !ptr16(vq) || !ptr16(o) || (reinterpret_cast<uintptr_t>(scales) & 3u))
+    return SA_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using namespace sa::flash;
+  int rc;
+  if (D == 32)
+    rc = launch_fwd<32, true, false, true>(q8, k8, vq, o, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
+                                           o_strides, scale, window_size, st, scales);
+  else if (D == 64)
+    rc = launch_fwd<64, true, false, true>(q8, k8, vq, o, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
+                                           o_strides, scale, window_size, st, scales);
+  else
+    rc = launch_fwd<128, true, false, true>(q8, k8, vq, o, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
+                                            o_strides, scale, window_size, st, scales);
   if (rc != SA_OK) return rc;
   return sa_record_cuda_error(cudaGetLastError());
 }

@@ -109,7 +109,7 @@ int launch_rope(const RopeTensor& a, const RopeTensor& b, const void* cosv, cons
   return sa_record_cuda_error(cudaGetLastError());
 }
 
-bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_rope_args(const void* x, const int64_t* s, const void* cosv, const void* sinv, int cs_dtype, int64_t T,
                     int64_t D, int dtype) {

@@ -55,6 +55,9 @@ SIGNATURES = {
     "sa_rope_flash_fwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _int, _p, _i64,
                                  _i64, _i64, _i64, _i64, _i64, _i64p, _i64p, _i64p, _i64p,
                                  _f, _i64, _int, _int, _p]),
+    "sa_fp8_quantize": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p, _p, _p, _p, _p, _p]),
+    "sa_fp8_flash_fwd": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                _i64p, _i64p, _i64p, _i64p, _f, _i64, _p]),
     "sa_paged_decode_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
     "sa_paged_decode": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64,
                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f, _int, _p]),

@@ -610,7 +610,61 @@ def sp2norm_rope_flash_attention_proj(q, k, v, w_o, cos, sin, *, scale=None, win
     _rope_flash_fwd(q, k, v, cos, sin, scale, window_size, o=o_bthd.permute(0, 2, 1, 3))
     w = w_o.to(device=q.device, dtype=q.dtype).reshape(H_q * D, D_model)
     return torch.matmul(o_bthd.view(B * T, H_q * D), w).view(B, T, D_model).to(torch.bfloat16)
-sp2norm_fp8_flash_attention = _not_built("sp2norm_fp8_flash_attention", "kernels.py:2630-2673")
+def _fp8_quantize(q, k, v):
+    """Per-tensor E4M3 quantization of q, k, v on the device (sa_fp8_quantize;
+    the reference's _quantize_to_fp8, kernels.py:2592-2601, without its
+    host synchronisation).  Returns (q8, k8, vq, scales): E4M3 bytes as
+    uint8 tensors, v's quantized values as bf16, device float[3] scales."""
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    dev = q.device
+    q8 = torch.empty(q.shape, device=dev, dtype=torch.uint8)
+    k8 = torch.empty(k.shape, device=dev, dtype=torch.uint8)
+    vq = torch.empty(v.shape, device=dev, dtype=torch.bfloat16)
+    scales = torch.empty(3, device=dev, dtype=torch.float32)
+    amax = torch.empty(3, device=dev, dtype=torch.int32)
+    with torch.cuda.device(dev):
+        st = _lib.load().sa_fp8_quantize(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.numel(), k.numel(), v.numel(),
+                                         _DTYPE_CODE[q.dtype], q8.data_ptr(), k8.data_ptr(), vq.data_ptr(),
+                                         scales.data_ptr(), amax.data_ptr(), _stream(q))
+    _lib.check(st, "sa_fp8_quantize")
+    return q8, k8, vq, scales
+
+
+def sp2norm_fp8_flash_attention(q, k, v, *, scale=None, window_size=0):
+    """FP8 fused flash attention forward (kernels.py:2630-2673).
+
+    q, k, v are quantized per tensor to E4M3 on the device; QK^T runs on FP8
+    tensor cores (tcgen05 kind::f8f6f4) with the dequantization scales folded
+    into the score scale, the squareplus activation in fp32, P.V on bf16
+    tensor cores against v's quantized values, times v's scale.  Returns
+    [B, H_q, T, D] bf16.
+    """
+    assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
+    assert k.shape == (B, H_kv, T, D) and v.shape == (B, H_kv, T, D)
+    assert H_q % H_kv == 0, f"H_q ({H_q}) must be divisible by H_kv ({H_kv})"
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _validate_cuda_tensor(t, name=name)
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError(f"q/k/v must share one dtype, got {q.dtype}/{k.dtype}/{v.dtype}")
+    if D not in FLASH_HEAD_DIMS:
+        raise ValueError(f"head dim {D} not supported (supported: {FLASH_HEAD_DIMS})")
+    o = torch.empty(B, H_q, T, D, device=q.device, dtype=torch.bfloat16)
+    if q.numel() == 0:
+        return o
+    q8, k8, vq, scales = _fp8_quantize(q, k, v)
+    row_sums = torch.empty(B, H_q, T, device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        st = _lib.load().sa_fp8_flash_fwd(
+            q8.data_ptr(), k8.data_ptr(), vq.data_ptr(), o.data_ptr(), row_sums.data_ptr(), scales.data_ptr(),
+            B, H_q, H_kv, T, D, _lib.strides(q8), _lib.strides(k8), _lib.strides(vq), _lib.strides(o),
+            float(scale), int(window_size), _stream(q),
+        )
+    _lib.check(st, "sa_fp8_flash_fwd")
+    return o
 
 
 # ---------------------------------------------------------------------------

@@ -17,6 +17,7 @@ in float32 with seeded ``torch.Generator`` inputs:
     ``apply_rope_eager`` (tests/test_rope_proj.py:15-30) followed by
     ``sp2norm_flash_attention_eager``, and the per-head projection sum of
     tests/test_rope_proj.py:134-138
+  * ``_quantize_to_fp8`` (kernels.py:2592-2601): E4M3 values and scales
 
 and writes ``golden.npz`` next to this script.  The GPU box never runs this
 script (the reference is not present there); the tests only read the
@@ -174,6 +175,18 @@ def main():
                 proj += torch.matmul(o_bf16[:, h].float(), w_o[h].float())
             data[f"{name}/w_o"] = w_o.float().numpy()
             data[f"{name}/proj"] = proj.numpy()
+
+    # --- FP8 per-tensor quantization (kernels.py:2592-2601) -----------------
+    from smooth_attn.kernels import _quantize_to_fp8  # noqa: E402
+
+    fp8_cases = [("fp8_bf16", (2, 4, 64, 32), torch.bfloat16, 1.0), ("fp8_f32", (1, 2, 48, 64), torch.float32, 7.5),
+                 ("fp8_tiny", (1, 1, 16, 32), torch.float32, 1e-3)]
+    for i, (name, shape, dt, mag) in enumerate(fp8_cases):
+        x = (randn(shape, 9500 + i) * mag).to(dt)
+        x8, sc = _quantize_to_fp8(x)
+        data[f"{name}/x"] = x.float().numpy()
+        data[f"{name}/x8"] = x8.float().numpy()
+        data[f"{name}/scale"] = np.array(sc, dtype=np.float64)
 
     np.savez_compressed(OUT, **data)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(data)} arrays)")

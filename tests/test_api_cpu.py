@@ -89,9 +89,17 @@ def test_bad_implementation():
         sa.softplus_norm_causal(torch.zeros(4, 4), implementation="cuda")
 
 
-def test_not_built_extensions_raise():
-    with pytest.raises(NotImplementedError):
-        sa.sp2norm_fp8_flash_attention(None)
+def test_extensions_refuse_host_tensors():
+    """RoPE / FP8 / paged entry points exist under the reference's names and
+    refuse CPU tensors (there is no CPU fallback)."""
+    q = torch.zeros(1, 2, 64, 32, dtype=torch.bfloat16)
+    cos, sin = sa.precompute_rope_cos_sin(32, 64, device="cpu")
+    with pytest.raises(ValueError, match="CUDA"):
+        sa.sp2norm_fp8_flash_attention(q, q, q)
+    with pytest.raises(ValueError, match="CUDA"):
+        sa.sp2norm_rope_flash_attention(q, q, q, cos, sin)
+    with pytest.raises(ValueError, match="CUDA"):
+        sa.sp2norm_rope_flash_attention_proj(q, q, q, torch.zeros(2, 32, 64), cos, sin)
 
 
 def test_paged_decode_rejects_cpu_tensors():
