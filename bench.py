@@ -432,6 +432,25 @@ def run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind):
     out["rope_flash_fwd"] = {"config": "RoPE + causal squareplus attention forward, bf16, public API per call",
                              "per_shape": rope}
     torch.cuda.empty_cache()
+
+    # FP8 attention forward (device quantization + E4M3 QK^T forward) vs the bf16 forward
+    f8 = {}
+    for B, H, T, D in ((4, 8, 1024, 64), (2, 32, 8192, 128)):
+        q, k, v = (torch.randn(B, H, T, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+        fl = O.flash_flops(B, H, T, D)
+        row = {}
+        for name, fn in (("fp8", lambda: sa.sp2norm_fp8_flash_attention(q, k, v)),
+                         ("bf16", lambda: sa.sp2norm_flash_attention(q, k, v))):
+            for _ in range(3):
+                fn()
+            n = 20
+            ms = time_steps(fn, n, world) / n
+            row[name] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1)}
+        f8[f"B={B} H={H} T={T} D={D}"] = row
+        del q, k, v
+    out["fp8_flash_fwd"] = {"config": "FP8 (E4M3 QK^T) causal squareplus attention forward incl. quantization, "
+                                      "public API per call; bf16 forward beside it", "per_shape": f8}
+    torch.cuda.empty_cache()
     return out
 
 
