@@ -18,13 +18,15 @@ int flash_timeouts(int reset);      // flash_fwd.cu
 int flash_bwd_timeouts(int reset);  // flash_bwd.cu
 int paged_timeouts(int reset);      // paged.cu
 int paged_bad_pages(int reset);     // paged.cu
+int paged_tc_timeouts(int reset);   // paged_tc.cu
+int paged_tc_bad_pages(int reset);  // paged_tc.cu
 }  // namespace sa
 
 extern "C" int sa_device_status(int reset) {
   if (cudaDeviceSynchronize() != cudaSuccess) return sa_record_cuda_error(cudaGetLastError());
   const int n = sa::norm_timeouts(reset) + sa::flash_timeouts(reset) + sa::flash_bwd_timeouts(reset) +
-                sa::paged_timeouts(reset);
-  const int bad = sa::paged_bad_pages(reset);
+                sa::paged_timeouts(reset) + sa::paged_tc_timeouts(reset);
+  const int bad = sa::paged_bad_pages(reset) + sa::paged_tc_bad_pages(reset);
   return n ? SA_ERR_TIMEOUT : bad ? SA_ERR_ARG : SA_OK;
 }
 

@@ -43,6 +43,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <stdlib.h>
+#include <string.h>
+
 #include <algorithm>
 #include <mutex>
 #include <type_traits>
@@ -53,6 +56,14 @@
 int sa_record_cuda_error(cudaError_t e);
 
 namespace sa {
+
+// tensor-core variant (paged_tc.cu)
+bool paged_tc_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks, int64_t bs, int64_t D, int dtype,
+                   int sms, int* GT, int64_t* grid, int* slots, int64_t* ticket_bytes, int64_t* part_bytes);
+int paged_tc_launch(const void* q, const void* k_cache, const void* v_cache, void* out, const int32_t* bt,
+                    const int32_t* cl, void* workspace, int64_t B, int64_t Hq, int64_t Hkv, int64_t num_blocks,
+                    int64_t bs, int64_t max_blocks, float scale, int GT, int64_t grid, int slots,
+                    int64_t ticket_bytes, cudaStream_t st);
 
 static __device__ unsigned g_paged_timeouts;  // bounded-wait failures (never traps)
 static __device__ unsigned g_paged_bad_pages; // block_table entries outside [0, num_blocks)
@@ -392,10 +403,19 @@ __global__ void __launch_bounds__(kPgWarps * 32) paged_decode_kernel(const Paged
     const int nsl = (int)(i1 - i0 + 1);
     float* sy = &red[0][0];  // reuse: GT sums of 4y
     __syncthreads();
-    if (threadIdx.x < GT) {
-      float t = 0.f;
-      for (int sl = 0; sl < nsl; ++sl) t += __ldcg(base + (int64_t)sl * REC + GT * D + threadIdx.x);
-      sy[GT * D + threadIdx.x] = t + eps4;
+    if (threadIdx.x < 32) {  // one warp: lanes stride the slots, then a shuffle sum per head
+      float t[GT];
+#pragma unroll
+      for (int g = 0; g < GT; ++g) t[g] = 0.f;
+      for (int sl = threadIdx.x; sl < nsl; sl += 32)
+#pragma unroll
+        for (int g = 0; g < GT; ++g) t[g] += __ldcg(base + (int64_t)sl * REC + GT * D + g);
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) t[g] += __shfl_xor_sync(0xffffffffu, t[g], m);
+        if (threadIdx.x == 0) sy[GT * D + g] = t[g] + eps4;
+      }
     }
     __syncthreads();
     for (int e4 = threadIdx.x; e4 < GT * D / 4; e4 += NT) {
@@ -474,7 +494,17 @@ struct Plan {
   int64_t units, W, grid;
   size_t smem;
   int64_t ticket_bytes, part_bytes;
+  bool tc;  // tensor-core kernel (paged_tc.cu) instead of paged_decode_kernel
 };
+
+// SA_PAGED_DECODE_KERNEL=simt forces the CUDA-core kernel, =tc the
+// tensor-core one where the shape allows it; default: tensor cores for GQA
+// groups of bf16 D=128 caches with block_size a multiple of 8 dividing 128.
+int kernel_choice() {
+  const char* v = getenv("SA_PAGED_DECODE_KERNEL");
+  if (v && strcmp(v, "simt") == 0) return 0;
+  return 1;
+}
 
 // Resident CTAs per SM of one instantiation at one dynamic smem size, and
 // the one-time opt-in to that much dynamic shared memory, cached per device
@@ -547,6 +577,9 @@ int make_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks, int64_t bs
   if (D != 32 && D != 64 && D != 128 && D != 256) return SA_ERR_UNSUPPORTED;
   if (B > (1 << 24) || Hq > (1 << 20) || bs > (1 << 16) || max_blocks * bs > ((int64_t)1 << 30))
     return SA_ERR_UNSUPPORTED;
+  p->tc = kernel_choice() == 1 && paged_tc_plan(B, Hq, Hkv, max_blocks, bs, D, dtype, sm_count(), &p->GT,
+                                                  &p->grid, &p->slots, &p->ticket_bytes, &p->part_bytes);
+  if (p->tc) return SA_OK;
   const int G = (int)(Hq / Hkv);
   int GT = G & -G;  // largest power of two dividing G
   GT = std::min(GT, std::min(8, (int)D / 8));
@@ -638,6 +671,10 @@ extern "C" int sa_paged_decode(const void* q, const void* k_cache, const void* v
   if (!sa::al16(q) || !sa::al16(k_cache) || !sa::al16(v_cache) || !sa::al16(out)) return SA_ERR_ALIGN;
   if (!workspace || workspace_bytes < p.ticket_bytes + p.part_bytes) return SA_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_ALIGN;
+  if (p.tc)
+    return sa::paged_tc_launch(q, k_cache, v_cache, out, block_table, context_lens, workspace, B, Hq, Hkv,
+                               num_blocks, block_size, max_blocks, scale, p.GT, p.grid, p.slots, p.ticket_bytes,
+                               static_cast<cudaStream_t>(stream));
   sa::PagedArgs a;
   a.q = q;
   a.kc = k_cache;

@@ -195,6 +195,23 @@ def test_paged_bad_page_index_reported():
     assert lib.sa_device_status(0) == _lib.SA_OK
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,T,bs", [(2, 32, 8, 1000, 16), (1, 16, 2, 4100, 8), (3, 12, 4, 517, 32),
+                                           (1, 64, 4, 300, 64), (2, 8, 4, 129, 128), (4, 40, 2, 2222, 16)])
+def test_paged_tensor_core_and_simt_kernels(monkeypatch, B, Hq, Hkv, T, bs):
+    """bf16 D=128 GQA shapes run on the tensor-core kernel by default; the
+    CUDA-core kernel (SA_PAGED_DECODE_KERNEL=simt) must agree, and both match
+    the oracle (ragged last tiles, NaN-filled unused page rows, G up to 20)."""
+    q, kc, vc, bt, cl = _case(B, Hq, Hkv, T, 128, bs, seed=B * T + bs, fill=float("nan"))
+    cl = torch.tensor([max(1, T - 37 * i) for i in range(B)], dtype=torch.int32, device=CUDA)
+    ref = _ref(q, kc.nan_to_num(0.0), vc.nan_to_num(0.0), bt, cl)
+    out_tc = sa.sp2norm_paged_attention(q, kc, vc, bt, cl, block_size=bs)
+    monkeypatch.setenv("SA_PAGED_DECODE_KERNEL", "simt")
+    out_simt = sa.sp2norm_paged_attention(q, kc, vc, bt, cl, block_size=bs)
+    _check(out_tc, ref)
+    _check(out_simt, ref)
+    assert (out_tc.float() - out_simt.float()).abs().max() <= 2e-2
+
+
 def test_paged_rejects_bad_arguments():
     q, kc, vc, bt, cl = _case(1, 4, 4, 64, 64, 16, seed=4)
     with pytest.raises(AssertionError):
