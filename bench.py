@@ -177,6 +177,18 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"metric": "fused squareplus-attn fwd+bwd TFLOP/s", "n_gpus": world, **flash}), flush=True)
         return
+    if args.only in ("decode", "rope", "fp8"):  # one extension workload (profiling entry point)
+        g = torch.Generator(device="cuda").manual_seed(777 + rank)
+        shape = tuple(int(v) for v in args.shape.split(",")) if args.shape else None
+        if args.only == "decode":
+            res = extra_decode((shape,) if shape else DECODE_SHAPES, args.steps, world, g, hbm, O)
+        elif args.only == "rope":
+            res = extra_rope((shape,) if shape else ROPE_SHAPES, args.steps, world, g)
+        else:
+            res = extra_fp8((shape,) if shape else FP8_SHAPES, args.steps, world, g)
+        if rank == 0:
+            print(json.dumps({"workload": args.only, "n_gpus": world, "steps": args.steps, **res}), flush=True)
+        return
     B, H, L = args.norm_batch, NORM_CFG["H"], NORM_CFG["L"]
     m_loc = B * H  # this rank's block of the global [N*B, H, L, L] batch
     M = m_loc * world
@@ -385,57 +397,87 @@ def run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind):
     del q, k, v
     torch.cuda.empty_cache()
 
-    # paged-KV decode: GB/s of K+V bytes read, one call per step through the
-    # public API (host wrapper included), back to back
+    out["paged_decode"] = extra_decode(DECODE_SHAPES, 50, world, g, hbm, O)
+    torch.cuda.empty_cache()
+    out["rope_flash_fwd"] = extra_rope(ROPE_SHAPES, 20, world, g)
+    torch.cuda.empty_cache()
+    out["fp8_flash_fwd"] = extra_fp8(FP8_SHAPES, 20, world, g)
+    torch.cuda.empty_cache()
+    return out
+
+
+# the reference's decode benchmark shapes (tests/test_paged_long_context.py:115-137), block 16
+DECODE_SHAPES = ((1, 32, 8, 8192, 128, 16), (1, 32, 8, 32768, 128, 16), (8, 32, 8, 8192, 128, 16),
+                 (32, 32, 8, 1024, 128, 16), (1, 12, 12, 32768, 64, 16), (8, 32, 32, 8192, 128, 16),
+                 (64, 32, 8, 4096, 128, 16))
+ROPE_SHAPES = ((2, 32, 1024, 128), (4, 12, 512, 64), (2, 32, 8192, 128))  # tests/test_rope_proj.py:162-163 + long
+FP8_SHAPES = ((4, 8, 1024, 64), (2, 32, 8192, 128))  # tests/test_fp8_flash.py:126-127 + long
+
+
+def _gbs(nbytes, ms):
+    return round(nbytes / (ms * 1e-3) / 1e9, 1)
+
+
+def extra_decode(shapes, steps, world, g, hbm, O):
+    """Paged-KV decode: GB/s of K+V bytes read, one public-API call per step,
+    back to back; the B=1 T=8192 shape is spot-checked against the oracle."""
+    import smooth_attn as sa
+
+    dev = torch.device("cuda")
     dec = {}
-    for B, Hq, Hkv, T, D in ((1, 32, 8, 8192, 128), (1, 32, 8, 32768, 128), (8, 32, 8, 8192, 128),
-                             (32, 32, 8, 1024, 128), (1, 12, 12, 32768, 64), (8, 32, 32, 8192, 128)):
-        BS = 16
+    for B, Hq, Hkv, T, D, BS in shapes:
         nb = B * T // BS
         q = torch.randn(B, Hq, 1, D, device=dev, generator=g).to(torch.bfloat16)
         kc = torch.randn(nb, Hkv, BS, D, device=dev, generator=g).to(torch.bfloat16)
         vc = torch.randn(nb, Hkv, BS, D, device=dev, generator=g).to(torch.bfloat16)
         bt = torch.randperm(nb, device=dev, generator=g).to(torch.int32).view(B, -1)
         cl = torch.full((B,), T, dtype=torch.int32, device=dev)
-        f = lambda: sa.sp2norm_paged_attention(q, kc, vc, bt, cl, block_size=BS)
+        f = lambda: sa.sp2norm_paged_attention(q, kc, vc, bt, cl, block_size=BS)  # noqa: E731
         for _ in range(3):
             f()
-        n = 50
-        ms = time_steps(f, n, world) / n
+        ms = time_steps(f, steps, world) / steps
         b = B * T * Hkv * D * 4
-        key = f"B={B} H={Hq}/{Hkv} T={T} D={D}"
-        dec[key] = {"us": round(ms * 1e3, 1), "GB/s": gbs(b, ms), "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 3),
-                    "kv_bytes": b, "inputs_vs_L2": "larger" if b > 126e6 else "smaller (L2-resident, warm)"}
+        key = f"B={B} H={Hq}/{Hkv} T={T} D={D} bs={BS}"
+        dec[key] = {"us": round(ms * 1e3, 1), "GB/s": _gbs(b, ms), "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 3),
+                    "kv_bytes": b, "inputs_vs_L2": "larger" if b > 126e6 else "smaller (L2-resident, warm)",
+                    "kernel": "tcgen05" if (Hq // Hkv >= 2 and D == 128) else "cuda-core"}
         if B == 1 and T == 8192:
             o = f()
             ref = O.paged_decode_attention(q.float().cpu().numpy(), kc.float().cpu().numpy(),
                                            vc.float().cpu().numpy(), bt.cpu().numpy(), cl.cpu().numpy())
             dec[key]["max_abs_err_vs_oracle"] = float(np.abs(o.float().cpu().numpy() - ref).max())
         del q, kc, vc, bt, cl
-    out["paged_decode"] = {"config": "paged KV decode, bf16, block_size 16, shuffled pages, public API per call",
-                           "per_shape": dec}
-    torch.cuda.empty_cache()
+    return {"config": "paged KV decode, bf16, shuffled pages, public API per call", "per_shape": dec}
 
-    # RoPE attention forward (rotation pass + tcgen05 forward), TFLOP/s of the attention
+
+def extra_rope(shapes, steps, world, g):
+    """RoPE attention forward (rotation pass + tcgen05 forward), TFLOP/s of the attention."""
+    import smooth_attn as sa
+    from oracle import sa_oracle as O
+
+    dev = torch.device("cuda")
     rope = {}
-    for B, H, T, D in ((2, 32, 1024, 128), (4, 12, 512, 64), (2, 32, 8192, 128)):
+    for B, H, T, D in shapes:
         q, k, v = (torch.randn(B, H, T, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
         cos, sin = sa.precompute_rope_cos_sin(D, T, device=dev)
-        f = lambda: sa.sp2norm_rope_flash_attention(q, k, v, cos, sin)
+        f = lambda: sa.sp2norm_rope_flash_attention(q, k, v, cos, sin)  # noqa: E731
         for _ in range(3):
             f()
-        n = 20
-        ms = time_steps(f, n, world) / n
+        ms = time_steps(f, steps, world) / steps
         fl = O.flash_flops(B, H, T, D)
         rope[f"B={B} H={H} T={T} D={D}"] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1)}
         del q, k, v
-    out["rope_flash_fwd"] = {"config": "RoPE + causal squareplus attention forward, bf16, public API per call",
-                             "per_shape": rope}
-    torch.cuda.empty_cache()
+    return {"config": "RoPE + causal squareplus attention forward, bf16, public API per call", "per_shape": rope}
 
-    # FP8 attention forward (device quantization + E4M3 QK^T forward) vs the bf16 forward
+
+def extra_fp8(shapes, steps, world, g):
+    """FP8 attention forward (device quantization + E4M3 QK^T forward) beside the bf16 forward."""
+    import smooth_attn as sa
+    from oracle import sa_oracle as O
+
+    dev = torch.device("cuda")
     f8 = {}
-    for B, H, T, D in ((4, 8, 1024, 64), (2, 32, 8192, 128)):
+    for B, H, T, D in shapes:
         q, k, v = (torch.randn(B, H, T, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
         fl = O.flash_flops(B, H, T, D)
         row = {}
@@ -443,15 +485,12 @@ def run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind):
                          ("bf16", lambda: sa.sp2norm_flash_attention(q, k, v))):
             for _ in range(3):
                 fn()
-            n = 20
-            ms = time_steps(fn, n, world) / n
+            ms = time_steps(fn, steps, world) / steps
             row[name] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1)}
         f8[f"B={B} H={H} T={T} D={D}"] = row
         del q, k, v
-    out["fp8_flash_fwd"] = {"config": "FP8 (E4M3 QK^T) causal squareplus attention forward incl. quantization, "
-                                      "public API per call; bf16 forward beside it", "per_shape": f8}
-    torch.cuda.empty_cache()
-    return out
+    return {"config": "FP8 (E4M3 QK^T) causal squareplus attention forward incl. quantization, "
+                      "public API per call; bf16 forward beside it", "per_shape": f8}
 
 
 CPU_BLOCK_ROWS = 128  # CPU sample unit: a 128-row block of one [2048, 2048] causal matrix
@@ -534,8 +573,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--skip-flash", action="store_true")
-    ap.add_argument("--only", choices=("all", "norm", "flash"), default="all",
+    ap.add_argument("--only", choices=("all", "norm", "flash", "decode", "rope", "fp8"), default="all",
                     help="run one workload only (small-case profiling)")
+    ap.add_argument("--shape", default=None,
+                    help="with --only decode: B,Hq,Hkv,T,D,block_size; rope / fp8: B,H,T,D (one shape)")
     ap.add_argument("--norm-batch", type=int, default=NORM_CFG["B"],
                     help="B of the causal-norm workload [B,16,2048,2048] (BASELINE: 8)")
     ap.add_argument("--flash-shape", default=",".join(str(FLASH_CFG[k]) for k in "BHTD"),

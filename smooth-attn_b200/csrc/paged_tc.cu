@@ -498,6 +498,7 @@ bool paged_tc_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks, int64
   if (bs % 8 != 0 || ptc::TOK % bs != 0) return false;
   int gt = (int)std::min<int64_t>(G, ptc::NH);
   while (G % gt != 0) --gt;
+  if (gt < 2) return false;  // e.g. a prime group above 16: one head per MMA column is the CUDA-core case
   const int64_t units = B * Hkv * (G / gt);
   const int64_t M = (max_blocks * bs + ptc::TOK - 1) / ptc::TOK;
   if (units > INT32_MAX / 2 || M > INT32_MAX / 2) return false;
