@@ -172,6 +172,24 @@ SA_API int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, con
                                 int dtype, void* stream);
 
 /*
+ * Forward of a block of Tq queries at global positions q_offset ..
+ * q_offset+Tq-1 against keys / values at positions 0 .. Tk-1, with
+ * sa_flash_fwd's causal / window rule in global positions (a query at
+ * position p sees keys k <= p, p - k < window).  q, o: [B, Hq, Tq, D];
+ * k, v: [B, Hkv, Tk, D]; rowsum: fp32 [B, Hq, Tq]; other arguments as
+ * sa_flash_fwd (which is this call with Tq = Tk = T, q_offset = 0).  The
+ * building block of context parallelism: every rank runs its query chunks
+ * against the all-gathered key prefix; with a plain-sum normalizer no
+ * cross-rank rescaling is needed.  (No reference counterpart: the reference
+ * has no sequence parallelism.)
+ */
+SA_API int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B,
+                              int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk, int64_t q_offset, int64_t D,
+                              const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+                              const int64_t* o_strides, float scale, int64_t window_size, int exact_math,
+                              int dtype, void* stream);
+
+/*
  * Rotary position embedding, rotate-half form, rounded to the input type:
  *   out[..., i] = x1 c - x2 s,  out[..., i + D/2] = x2 c + x1 s
  * with x1 = x[..., i], x2 = x[..., i + D/2], c = cos[t, i], s = sin[t, i],

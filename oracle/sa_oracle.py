@@ -177,6 +177,31 @@ def _flash_mask(T, window_size):
     return m
 
 
+def chunk_flash_attention(q, k, v, q_offset, scale=None, window_size=0, acc=np.float32):
+    """Squareplus attention of a block of Tq queries at global positions
+    q_offset .. q_offset+Tq-1 over keys 0 .. Tk-1 (same causal / window rule
+    as kernels.py:2053-2084 in global positions).  With q_offset = 0 and
+    Tq = Tk it is sp2norm_flash_attention; a sequence split into query
+    chunks, each attending to the key prefix, reproduces the whole."""
+    q = _as_f(q, acc)
+    k = _expand_kv(_as_f(k, acc), q.shape[1])
+    v = _expand_kv(_as_f(v, acc), q.shape[1])
+    Tq, Tk, D = q.shape[-2], k.shape[-2], q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    qp = np.arange(Tq)[:, None] + q_offset
+    kp = np.arange(Tk)[None, :]
+    m = kp <= qp
+    if window_size > 0:
+        m &= (qp - kp) < window_size
+    s = np.matmul(q, np.swapaxes(k, -1, -2)) * acc(scale)
+    a = acc(2.0) * s - acc(1.0)
+    sp = acc(0.5) * (a + np.sqrt(a * a + acc(4.0)))
+    y = np.where(m, sp * sp, acc(0.0))
+    r = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    return np.matmul(y / r, v)
+
+
 def sp2norm_flash_attention(q, k, v, scale=None, window_size=0, acc=np.float32, return_rowsum=False):
     """Eager squareplus attention (kernels.py:2053-2084).
 

@@ -72,6 +72,7 @@ struct FwdParams {
   float* rowsum;
   int64_t so_b, so_h, so_s;
   int B, Hq, Hkv, T, npairs, window;
+  int Tk, qoff;         // key length; global position of query row 0 (keys start at 0)
   float scale2;         // 2 * scale
   const float* dscale;  // QK8: device {q_scale, k_scale, v_scale}; scores also scale by q_scale * k_scale
 };
@@ -107,17 +108,19 @@ __device__ __forceinline__ bool warp_wait_or_flag(uint64_t* bar, uint32_t phase,
   return ok;
 }
 
-// KV tile range [j0, j1) seen by the 128 query rows starting at q0.
-__device__ __forceinline__ void kv_range(int q0, int T, int window, int& j0, int& j1) {
-  const int nkv = (T + 127) / 128;
-  j1 = (q0 + 128 + 127) / 128;
+// KV tile range [j0, j1) seen by the 128 query rows starting at local row q0
+// (global position q0 + qoff) of a Tq-row query block over Tk keys.
+__device__ __forceinline__ void kv_range(int q0, int Tq, int qoff, int Tk, int window, int& j0, int& j1) {
+  const int q0g = q0 + qoff;
+  const int nkv = (Tk + 127) / 128;
+  j1 = (q0g + 128 + 127) / 128;
   if (j1 > nkv) j1 = nkv;
   j0 = 0;
   if (window > 0) {
-    const int first = q0 - window + 1;
+    const int first = q0g - window + 1;
     j0 = first > 0 ? first / 128 : 0;
   }
-  if (q0 >= T) j1 = j0;  // tile wholly past the sequence end: no work
+  if (q0 >= Tq || j1 < j0) j1 = j0;  // tile wholly past the query block, or no key in its window
 }
 
 // squareplus of one 32-column chunk already in registers; writes the
@@ -192,8 +195,8 @@ __global__ void __launch_bounds__(320, 1)
   const int qbase = pair * 2 * C::BM;
   // per Q tile KV ranges; the CTA streams the union
   int ja0, ja1, jb0, jb1;
-  kv_range(qbase, p.T, p.window, ja0, ja1);
-  kv_range(qbase + C::BM, p.T, p.window, jb0, jb1);
+  kv_range(qbase, p.T, p.qoff, p.Tk, p.window, ja0, ja1);
+  kv_range(qbase + C::BM, p.T, p.qoff, p.Tk, p.window, jb0, jb1);
   if (jb1 <= jb0) { jb0 = ja0; jb1 = ja0; }
   const int j0 = ja0 < jb0 ? ja0 : jb0;
   const int j1 = ja1 > jb1 ? ja1 : jb1;
@@ -343,8 +346,9 @@ __global__ void __launch_bounds__(320, 1)
     const int row = 32 * g + lane;
     const int q0 = qbase + t * C::BM;
     const int q = q0 + row;
+    const int q0g = q0 + p.qoff, qg = q + p.qoff;  // global query positions
     int jl, jh;
-    kv_range(q0, p.T, p.window, jl, jh);
+    kv_range(q0, p.T, p.qoff, p.Tk, p.window, jl, jh);
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     const uint32_t tS = tl + t * 128;
     float scale2 = p.scale2, vscale = 1.0f;
@@ -359,10 +363,10 @@ __global__ void __launch_bounds__(320, 1)
       if (!warp_wait_or_flag(&bars->s_full[t], it & 1, failed)) break;
       tc_fence_after();
       const int k0 = j * C::BN;
-      const bool need_mask = (k0 + C::BN - 1 > q0) || (k0 + C::BN > p.T) ||
-                             (p.window > 0 && q0 + C::BM - 1 - k0 >= p.window);
+      const bool need_mask = (k0 + C::BN - 1 > q0g) || (k0 + C::BN > p.Tk) ||
+                             (p.window > 0 && q0g + C::BM - 1 - k0 >= p.window);
       if (need_mask)
-        rsum += squareplus_row<BF16, EXACT, true>(tS, scale2, k0, q, p.T, p.window);
+        rsum += squareplus_row<BF16, EXACT, true>(tS, scale2, k0, qg, p.Tk, p.window);
       else
         rsum += squareplus_row<BF16, EXACT, false>(tS, scale2, 0, 0, 0, 0);
       tmem_st_wait();
@@ -446,12 +450,13 @@ template <int D, bool BF16, bool EXACT, bool QK8 = false>
 static int launch_fwd(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B, int64_t Hq,
                       int64_t Hkv, int64_t T, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                       const int64_t* os, float scale, int64_t window, cudaStream_t st,
-                      const float* dscale = nullptr) {
+                      const float* dscale = nullptr, int64_t Tk = -1, int64_t qoff = 0) {
   using C = FwdCfg<D, QK8>;
+  if (Tk < 0) Tk = T;
   CUtensorMap mq, mk, mv;
   if (!make_map_4d(&mq, q, BF16, B, Hq, T, D, qs, C::QK_CHUNK, C::BM, QK8) ||
-      !make_map_4d(&mk, k, BF16, B, Hkv, T, D, ks, C::QK_CHUNK, C::BN, QK8) ||
-      !make_map_4d(&mv, v, BF16, B, Hkv, T, D, vs, C::CHUNK, C::BN))
+      !make_map_4d(&mk, k, BF16, B, Hkv, Tk, D, ks, C::QK_CHUNK, C::BN, QK8) ||
+      !make_map_4d(&mv, v, BF16, B, Hkv, Tk, D, vs, C::CHUNK, C::BN))
     return SA_ERR_ALIGN;
   FwdParams p;
   p.o = o;
@@ -463,6 +468,8 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, floa
   p.Hq = (int)Hq;
   p.Hkv = (int)Hkv;
   p.T = (int)T;
+  p.Tk = (int)Tk;
+  p.qoff = (int)qoff;
   p.npairs = (int)((T + 2 * C::BM - 1) / (2 * C::BM));
   p.window = (int)window;
   p.scale2 = 2.0f * scale;
@@ -533,6 +540,49 @@ extern "C" int sa_flash_fwd(const void* q, const void* k, const void* v, void* o
   }
 #undef SA_FWD_D
 #undef SA_FWD_CASE
+  if (rc != SA_OK) return rc;
+  return sa_record_cuda_error(cudaGetLastError());
+}
+
+extern "C" int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void* o, float* rowsum,
+                                  int64_t B, int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk, int64_t q_offset,
+                                  int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                                  const int64_t* v_strides, const int64_t* o_strides, float scale,
+                                  int64_t window_size, int exact_math, int dtype, void* stream) {
+  if (dtype != SA_BF16 && dtype != SA_F16) return SA_ERR_UNSUPPORTED;
+  if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
+  if (B < 0 || Hq < 1 || Hkv < 1 || Tq < 0 || Tk < 0 || q_offset < 0 || Hq % Hkv != 0 || window_size < 0)
+    return SA_ERR_ARG;
+  if (B == 0 || Tq == 0) return SA_OK;
+  if (Tk == 0) return SA_ERR_ARG;  // every query must see at least one key
+  if (Tq > (1ll << 30) || Tk > (1ll << 30) || q_offset > (1ll << 30) || B * Hq > 65535) return SA_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !o || !rowsum) return SA_ERR_ARG;
+  if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides) || !strides_ok(o_strides))
+    return SA_ERR_ALIGN;
+  if (!ptr16(q) || !ptr16(k) || !ptr16(v) || !ptr16(o)) return SA_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using namespace sa::flash;
+  int rc;
+#define SA_FWDC_CASE(DD, BF, EX)                                                                                  \
+  rc = launch_fwd<DD, BF, EX>(q, k, v, o, rowsum, B, Hq, Hkv, Tq, q_strides, k_strides, v_strides, o_strides, \
+                              scale, window_size, st, nullptr, Tk, q_offset)
+#define SA_FWDC_D(DD)                                   \
+  if (dtype == SA_BF16) {                               \
+    if (exact_math) SA_FWDC_CASE(DD, true, true);       \
+    else SA_FWDC_CASE(DD, true, false);                 \
+  } else {                                              \
+    if (exact_math) SA_FWDC_CASE(DD, false, true);      \
+    else SA_FWDC_CASE(DD, false, false);                \
+  }
+  if (D == 32) {
+    SA_FWDC_D(32)
+  } else if (D == 64) {
+    SA_FWDC_D(64)
+  } else {
+    SA_FWDC_D(128)
+  }
+#undef SA_FWDC_D
+#undef SA_FWDC_CASE
   if (rc != SA_OK) return rc;
   return sa_record_cuda_error(cudaGetLastError());
 }

@@ -509,6 +509,40 @@ def sp2norm_flash_attention(q, k, v, *, scale=None, window_size=0, exact_math=Fa
     return _SP2NormFlashAttentionFn.apply(q, k, v, scale, H_q // H_kv, window_size, not exact_math)
 
 
+def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=0, exact_math=False):
+    """Forward of a block of queries against a key prefix (``sa_flash_fwd_chunk``).
+
+    q: [B, H_q, Tq, D] at global positions q_offset .. q_offset+Tq-1;
+    k, v: [B, H_kv, Tk, D] at positions 0 .. Tk-1.  Same causal (and window)
+    rule as ``sp2norm_flash_attention`` in global positions, so splitting a
+    sequence into query chunks that each see their key prefix reproduces the
+    whole forward.  The building block of context parallelism
+    (``smooth_attn.parallel.context_parallel_attention``).  Returns
+    (o [B, H_q, Tq, D], row_sums [B, H_q, Tq]).
+    """
+    assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
+    B, H_q, Tq, D = q.shape
+    H_kv, Tk = k.shape[1], k.shape[2]
+    assert k.shape == (B, H_kv, Tk, D) and v.shape == (B, H_kv, Tk, D)
+    assert H_q % H_kv == 0, f"H_q ({H_q}) must be divisible by H_kv ({H_kv})"
+    _flash_check(q, k, v)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
+    o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    row_sums = torch.empty(B, H_q, Tq, device=q.device, dtype=torch.float32)
+    if q.numel() == 0:
+        return o, row_sums
+    with torch.cuda.device(q.device):
+        st = _lib.load().sa_flash_fwd_chunk(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
+            B, H_q, H_kv, Tq, Tk, int(q_offset), D, _lib.strides(q), _lib.strides(k), _lib.strides(v),
+            _lib.strides(o), float(scale), int(window_size), int(bool(exact_math)), _DTYPE_CODE[q.dtype], _stream(q),
+        )
+    _lib.check(st, "sa_flash_fwd_chunk")
+    return o, row_sums
+
+
 # ---------------------------------------------------------------------------
 # forward-only extensions outside this build's hot path (kernels.py:2093-2829)
 # ---------------------------------------------------------------------------

@@ -7,6 +7,9 @@ heads).  Units are split into contiguous blocks, one per rank, and every
 rank runs the single-GPU kernels on its block; there is no collective on the
 data path.  ``gather_units`` collects the per-rank blocks (NCCL over NVLink on
 GPUs, gloo on CPU) for validation only.
+
+Context (sequence) parallelism for sequences too long for one GPU's block of
+heads is the one exchange step: ``context_parallel_attention`` (below).
 """
 
 from __future__ import annotations
@@ -76,3 +79,83 @@ def gather_units(local: torch.Tensor, n_units: int, group=None) -> torch.Tensor 
         parts = [torch.empty_like(pad) for _ in range(world)]
         dist.all_gather(parts, pad, group=group)
     return torch.cat([p[:c] for p, c in zip(parts, counts)])
+
+
+# ---------------------------------------------------------------------------
+# context parallelism: zig-zag sequence chunks, all-gathered K/V
+# ---------------------------------------------------------------------------
+
+
+def zigzag_chunk_ids(world: int, rank: int) -> tuple[int, int]:
+    """The two of the 2*world sequence chunks held by ``rank``: (rank,
+    2*world-1-rank).  Pairing an early chunk with a late one gives every rank
+    the same causal work (chunk c sees c+1 key chunks)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    return rank, 2 * world - 1 - rank
+
+
+def zigzag_split(x: torch.Tensor, world: int, rank: int, dim: int = 2) -> torch.Tensor:
+    """This rank's two zig-zag chunks of the sequence dim of ``x``, concatenated."""
+    T = x.shape[dim]
+    if T % (2 * world):
+        raise ValueError(f"sequence length {T} is not a multiple of 2*world = {2 * world}")
+    chunks = x.chunk(2 * world, dim=dim)
+    a, b = zigzag_chunk_ids(world, rank)
+    return torch.cat([chunks[a], chunks[b]], dim=dim)
+
+
+def zigzag_merge(parts, dim: int = 2) -> torch.Tensor:
+    """Inverse of ``zigzag_split`` over all ranks: ``parts[r]`` is rank r's
+    local tensor; returns the sequence in global order."""
+    world = len(parts)
+    chunks = [None] * (2 * world)
+    for r, p in enumerate(parts):
+        a, b = zigzag_chunk_ids(world, r)
+        chunks[a], chunks[b] = p.chunk(2, dim=dim)
+    return torch.cat(chunks, dim=dim)
+
+
+def _all_gather(x: torch.Tensor, group=None) -> list:
+    world = dist.get_world_size(group)
+    x = x.contiguous()
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x, group=group)
+        return list(out.unbind(0))
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x, group=group)
+    return parts
+
+
+def context_parallel_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=None, scale=None,
+                               window_size: int = 0) -> torch.Tensor:
+    """Causal squareplus attention forward with the sequence split over ranks.
+
+    q, k, v are this rank's zig-zag local blocks ``[B, H, 2C, D]`` (see
+    ``zigzag_split``; the global length is T = 2·C·world).  K and V are
+    all-gathered once (NCCL over NVLink on GPUs) and put back in sequence
+    order; each of the rank's two query chunks then runs the tcgen05 forward
+    against its visible key prefix (``sp2norm_flash_attention_chunk`` with the
+    chunk's global offset).  The squareplus normalizer is a plain sum, so no
+    cross-rank max or rescale is needed: the result equals the single-GPU
+    forward.  Returns the rank's output in the same zig-zag local layout.
+    Forward only (like the reference's RoPE / FP8 / paged entry points).
+    """
+    from . import kernels
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    Tl = q.shape[2]
+    if Tl % 2:
+        raise ValueError("the local sequence block must hold two equal zig-zag chunks")
+    C = Tl // 2
+    kv = torch.stack([k, v]).contiguous()
+    full = zigzag_merge(_all_gather(kv, group), dim=3)  # [2, B, Hkv, T, D] in sequence order
+    outs = []
+    for i, c in enumerate(zigzag_chunk_ids(world, rank)):
+        qc = q[:, :, i * C:(i + 1) * C]
+        kp, vp = full[0, :, :, :(c + 1) * C], full[1, :, :, :(c + 1) * C]
+        o, _ = kernels.sp2norm_flash_attention_chunk(qc, kp, vp, c * C, scale=scale, window_size=window_size)
+        outs.append(o)
+    return torch.cat(outs, dim=2)

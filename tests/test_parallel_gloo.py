@@ -13,7 +13,17 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from oracle import sa_oracle as O
-from smooth_attn.parallel import gather_units, shard_heads, shard_kv_groups, shard_units
+from smooth_attn.parallel import (
+    _all_gather,
+    context_parallel_attention,
+    gather_units,
+    shard_heads,
+    shard_kv_groups,
+    shard_units,
+    zigzag_chunk_ids,
+    zigzag_merge,
+    zigzag_split,
+)
 
 
 def test_shard_units_covers_everything_once():
@@ -36,6 +46,33 @@ def test_shard_kv_groups_keeps_gqa_groups_whole():
     assert torch.equal(qs[0], q[0, 4:8])
 
 
+def test_zigzag_split_merge_round_trip_and_balance():
+    x = torch.arange(2 * 3 * 24 * 2, dtype=torch.float32).reshape(2, 3, 24, 2)
+    for world in (1, 2, 3, 4):
+        parts = [zigzag_split(x, world, r) for r in range(world)]
+        assert torch.equal(zigzag_merge(parts), x)
+        # causal work of a rank = key chunks seen by its two query chunks: equal for all ranks
+        work = {sum(c + 1 for c in zigzag_chunk_ids(world, r)) for r in range(world)}
+        assert work == {2 * world + 1}
+    with pytest.raises(ValueError):
+        zigzag_split(x, 5, 0)
+
+
+@pytest.mark.parametrize("window", [0, 5, 40])
+def test_oracle_query_chunks_reproduce_full_attention(window):
+    """The restatement behind the chunk kernel: query chunks at their global
+    offset against the key prefix give the full causal forward."""
+    g = np.random.default_rng(3)
+    q = g.standard_normal((1, 4, 48, 16)).astype(np.float32)
+    k = g.standard_normal((1, 2, 48, 16)).astype(np.float32)
+    v = g.standard_normal((1, 2, 48, 16)).astype(np.float32)
+    full = O.sp2norm_flash_attention(q, k, v, window_size=window)
+    C = 12
+    parts = [O.chunk_flash_attention(q[:, :, c * C:(c + 1) * C], k[:, :, :(c + 1) * C], v[:, :, :(c + 1) * C],
+                                     c * C, window_size=window) for c in range(4)]
+    np.testing.assert_allclose(np.concatenate(parts, axis=2), full, rtol=1e-5, atol=1e-6)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -50,6 +87,26 @@ def _worker(rank, world, port, mode, q):
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
     try:
+        if mode.startswith("cp"):
+            # context parallelism: the gather / reorder / chunk logic, with the
+            # chunk kernel replaced by the oracle (CPU ranks, no GPU)
+            import smooth_attn.kernels as K
+
+            def chunk(qc, kp, vp, off, scale=None, window_size=0):
+                o = O.chunk_flash_attention(qc.numpy(), kp.numpy(), vp.numpy(), off, scale=scale,
+                                            window_size=window_size)
+                return torch.from_numpy(o), None
+
+            K.sp2norm_flash_attention_chunk = chunk
+            window = int(mode[2:] or 0)
+            g = torch.Generator().manual_seed(1)
+            qf, kf, vf = (torch.randn(2, h, 40, 8, generator=g) for h in (4, 2, 2))
+            o_local = context_parallel_attention(*(zigzag_split(t, world, rank) for t in (qf, kf, vf)),
+                                                 window_size=window)
+            o = zigzag_merge(_all_gather(o_local))
+            ref = O.sp2norm_flash_attention(qf.numpy(), kf.numpy(), vf.numpy(), window_size=window)
+            q.put((rank, "ok", float(np.abs(o.numpy() - ref).max())))
+            return
         g = torch.Generator().manual_seed(0)
         x = torch.randn(3, 5, 12, 12, generator=g)  # 15 units: uneven split
         if mode == "fail" and rank == 1:
@@ -93,3 +150,10 @@ def test_gloo_world2_rank_failure_surfaces_as_error():
     res = _run("fail")
     assert res[1][1] == "error"  # the failing rank
     assert res[0][1] == "error"  # the survivor's collective errors out instead of hanging
+
+
+@pytest.mark.parametrize("mode", ["cp", "cp7"])
+def test_gloo_world2_context_parallel_equals_single_process(mode):
+    res = _run(mode)
+    assert [r[1] for r in res] == ["ok", "ok"], res
+    assert all(r[2] < 1e-5 for r in res), res
