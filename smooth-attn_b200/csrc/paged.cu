@@ -50,20 +50,13 @@
 #include <mutex>
 #include <type_traits>
 
+#include "paged_tc.h"
 #include "sa_common.cuh"
 #include "smooth_attn_b200.h"
 
 int sa_record_cuda_error(cudaError_t e);
 
 namespace sa {
-
-// tensor-core variant (paged_tc.cu)
-bool paged_tc_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks, int64_t bs, int64_t D, int dtype,
-                   int sms, int* GT, int64_t* grid, int* slots, int64_t* ticket_bytes, int64_t* part_bytes);
-int paged_tc_launch(const void* q, const void* k_cache, const void* v_cache, void* out, const int32_t* bt,
-                    const int32_t* cl, void* workspace, int64_t B, int64_t Hq, int64_t Hkv, int64_t num_blocks,
-                    int64_t bs, int64_t max_blocks, float scale, int GT, int64_t grid, int slots,
-                    int64_t ticket_bytes, cudaStream_t st);
 
 static __device__ unsigned g_paged_timeouts;  // bounded-wait failures (never traps)
 static __device__ unsigned g_paged_bad_pages; // block_table entries outside [0, num_blocks)
@@ -495,6 +488,7 @@ struct Plan {
   size_t smem;
   int64_t ticket_bytes, part_bytes;
   bool tc;  // tensor-core kernel (paged_tc.cu) instead of paged_decode_kernel
+  PtcPlan ptc;
 };
 
 // SA_PAGED_DECODE_KERNEL=simt forces the CUDA-core kernel, =tc the
@@ -577,9 +571,12 @@ int make_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks, int64_t bs
   if (D != 32 && D != 64 && D != 128 && D != 256) return SA_ERR_UNSUPPORTED;
   if (B > (1 << 24) || Hq > (1 << 20) || bs > (1 << 16) || max_blocks * bs > ((int64_t)1 << 30))
     return SA_ERR_UNSUPPORTED;
-  p->tc = kernel_choice() == 1 && paged_tc_plan(B, Hq, Hkv, max_blocks, bs, D, dtype, sm_count(), &p->GT,
-                                                  &p->grid, &p->slots, &p->ticket_bytes, &p->part_bytes);
-  if (p->tc) return SA_OK;
+  p->tc = kernel_choice() == 1 && paged_tc_plan(B, Hq, Hkv, max_blocks, bs, D, dtype, sm_count(), &p->ptc);
+  if (p->tc) {
+    p->ticket_bytes = p->ptc.ticket_bytes;
+    p->part_bytes = p->ptc.part_bytes;
+    return SA_OK;
+  }
   const int G = (int)(Hq / Hkv);
   int GT = G & -G;  // largest power of two dividing G
   GT = std::min(GT, std::min(8, (int)D / 8));
@@ -673,8 +670,7 @@ extern "C" int sa_paged_decode(const void* q, const void* k_cache, const void* v
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_ALIGN;
   if (p.tc)
     return sa::paged_tc_launch(q, k_cache, v_cache, out, block_table, context_lens, workspace, B, Hq, Hkv,
-                               num_blocks, block_size, max_blocks, scale, p.GT, p.grid, p.slots, p.ticket_bytes,
-                               static_cast<cudaStream_t>(stream));
+                               num_blocks, block_size, max_blocks, scale, p.ptc, static_cast<cudaStream_t>(stream));
   sa::PagedArgs a;
   a.q = q;
   a.kc = k_cache;

@@ -33,6 +33,7 @@
 
 #include <algorithm>
 
+#include "paged_tc.h"
 #include "sa_sm100.cuh"
 #include "smooth_attn_b200.h"
 
@@ -60,7 +61,7 @@ constexpr int OFF_Q = 2 * NS * KT;   // 2 D-halves x 16 head rows x 128 B
 constexpr int OFF_P = OFF_Q + 4096;  // 2 buffers x 2 token-halves x 32 rows x 128 B
 constexpr int OFF_RED = OFF_P + 2 * 8192;
 constexpr int OFF_BAR = OFF_RED + 1024;
-constexpr int SMEM = OFF_BAR + 256 + 1024;  // + alignment slack
+constexpr int SMEM = OFF_BAR + 512 + 1024;  // + alignment slack
 constexpr int THREADS = 224;  // K producer, MMA, 4 squareplus warps, V producer
 constexpr uint32_t TMEM_COLS = 64;  // S^T x2 @0/@16, O^T @32
 
@@ -76,13 +77,18 @@ struct Args {
   float scale2;
 };
 
+constexpr int IQ = 4;  // item queue entries
+
 struct Bars {
   uint64_t k_full[NS], k_empty[NS], v_full[NS], v_empty[NS];
   uint64_t s_full[2], p_full[2], p_free[2];
   uint64_t q_full, o_full;
+  uint64_t it_full[IQ], it_empty[IQ];
+  int itq[IQ];
   uint32_t tmem_base;
   int last;
 };
+static_assert(sizeof(Bars) <= 512, "barrier block");
 
 // All waits poll (test_wait) instead of suspending: every tile passes four
 // hand-offs (TMA -> MMA -> squareplus -> MMA -> TMA) and a suspended
@@ -109,25 +115,36 @@ __device__ __forceinline__ bool wait_or(uint64_t* bar, uint32_t phase, bool& fai
 
 __device__ __forceinline__ void ew_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Unit decomposition shared by all roles.
+// A work item is one unit segment: tiles [t_lo, t_hi) of unit u (t_hi cut at
+// the context) inside the CTA's contiguous range of the flattened (unit,
+// tile) space, with its partial-record slot among the unit's nslots
+// contributing CTAs.  (Handing out unit-aligned chunks from an atomic counter
+// instead was measured slower on every shape: per-chunk epilogues and more
+// partials cost more than the static split's imbalance.)
 struct Unit {
-  int b, h, hq0, ctx, t_lo, t_hi;  // active tiles [t_lo, t_hi) of this CTA's range
-  bool whole;                      // the range covers the unit's every tile
+  int u, b, h, hq0, ctx, t_lo, t_hi, slot, nslots;
+  bool whole;  // the item covers the unit's every tile: output written directly
 };
 
-__device__ __forceinline__ Unit unit_of(const Args& a, int u, int64_t x0, int64_t x1) {
+__device__ __forceinline__ Unit item_of(const Args& a, int id, int64_t x0, int64_t x1) {
   Unit r;
+  r.u = id;
+  const int64_t ub = (int64_t)id * a.M;
+  const int64_t lo = max(x0, ub) - ub, hi = min(x1, ub + a.M) - ub;
+  const int64_t NC = gridDim.x;
+  const int64_t i0 = ((ub + 1) * NC - 1) / a.W;  // CTAs i0..i1 cover unit u
+  const int64_t i1 = (min(a.W, ub + a.M) * NC - 1) / a.W;
+  r.slot = (int)(blockIdx.x - i0);
+  r.nslots = (int)(i1 - i0 + 1);
   const int upb = a.Hkv * a.nhc;
-  r.b = u / upb;
-  const int rem = u - r.b * upb;
+  r.b = r.u / upb;
+  const int rem = r.u - r.b * upb;
   r.h = rem / a.nhc;
   r.hq0 = r.h * a.G + (rem - r.h * a.nhc) * a.GT;
   r.ctx = max(0, min(__ldg(a.cl + r.b), a.max_blocks * a.bs));
-  const int64_t ub = (int64_t)u * a.M;
-  const int lo = (int)(max(x0, ub) - ub), hi = (int)(min(x1, ub + a.M) - ub);
   r.whole = lo == 0 && hi == a.M;
-  r.t_lo = lo;
-  r.t_hi = min(hi, (r.ctx + TOK - 1) / TOK);
+  r.t_lo = (int)lo;
+  r.t_hi = (int)min(hi, (int64_t)((r.ctx + TOK - 1) / TOK));
   return r;
 }
 
@@ -140,7 +157,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t NC = gridDim.x, cta = blockIdx.x;
   const int64_t x0 = cta * a.W / NC, x1 = (cta + 1) * a.W / NC;
-  if (x0 >= x1) return;  // whole CTA, before any barrier
+  if (x0 >= x1) return;  // empty range, before any barrier
   const int u_first = (int)(x0 / a.M), u_last = (int)((x1 - 1) / a.M);
 
   if (threadIdx.x == 0) {
@@ -154,6 +171,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], 128);
       mbar_init(&bars->p_free[i], 1);
+    }
+    for (int i = 0; i < IQ; ++i) {
+      mbar_init(&bars->it_full[i], 1);
+      mbar_init(&bars->it_empty[i], 3);  // V producer, MMA issuer, epilogue warps
     }
     mbar_init(&bars->q_full, 128);
     mbar_init(&bars->o_full, 1);
@@ -173,6 +194,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   bool failed = false;
   const int np = TOK / a.bs;  // pages per tile
 
+  // Item queue: warp 0 publishes the ids of the CTA's units in order into a
+  // 4-entry ring; every role walks the same ring.
+  // take(k): the k-th item id of this CTA, -1 when there is no more work.
+  auto take = [&](int k, bool release) -> int {
+    const int sl = k % IQ;
+    if (!wait_uni(&bars->it_full[sl], (k / IQ) & 1, failed)) return -1;
+    const int id = bars->itq[sl];
+    __syncwarp();
+    if (release && lane == 0) mbar_arrive(&bars->it_empty[sl]);
+    return id;
+  };
+
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------------------ TMA producers
     // warp 0 streams K (stage freed by the S^T MMA), warp 6 streams V (freed
@@ -185,14 +218,27 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) tma_prefetch_desc(map);
     int n = 0;
     int wu = -1, wp = 0, win = 0;  // block-table window: lane l holds page wp + l of unit wu
-    for (int u = u_first; u <= u_last && !failed; ++u) {
-      const Unit U = unit_of(a, u, x0, x1);
+    for (int k = 0; !failed; ++k) {
+      int id;
+      if (!isv) {  // warp 0 publishes the k-th item
+        const int sl = k % IQ;
+        if (k >= IQ && !wait_uni(&bars->it_empty[sl], ((k / IQ) - 1) & 1, failed)) break;
+        if (lane == 0) {
+          bars->itq[sl] = u_first + k <= u_last ? u_first + k : -1;
+          mbar_arrive(&bars->it_full[sl]);
+        }
+        id = __shfl_sync(0xffffffffu, lane == 0 ? bars->itq[sl] : 0, 0);
+      } else {
+        id = take(k, true);
+      }
+      if (id < 0) break;
+      const Unit U = item_of(a, id, x0, x1);
       for (int ti = U.t_lo; ti < U.t_hi && !failed; ++ti, ++n) {
         const int s = n % NS;
         const int nload = min(np, (U.ctx - ti * TOK + a.bs - 1) / a.bs);
         const int p0 = ti * np;
-        if (wu != u || p0 < wp || p0 + nload > wp + 32) {  // refill: one load covers 32 / np tiles
-          wu = u;
+        if (wu != U.u || p0 < wp || p0 + nload > wp + 32) {  // refill: one load covers 32 / np tiles
+          wu = U.u;
           wp = p0;
           win = 0;
           if (wp + lane < a.max_blocks) win = __ldg(a.bt + (int64_t)U.b * a.max_blocks + wp + lane);
@@ -212,31 +258,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      constexpr uint32_t idesc_s = idesc_f16(128, NH, 1, 0, 0);
-      constexpr uint32_t idesc_o = idesc_f16(128, 2 * NH, 1, 1, 0);
-      const uint64_t dK0 = smem_desc(smem_u32(smem + OFF_K), 16, 1024, SW_128B);
-      const uint64_t dV0 = smem_desc(smem_u32(smem + OFF_V), HALF, 1024, SW_128B);
-      const uint64_t dQ0 = smem_desc(smem_u32(smem + OFF_Q), 16, 1024, SW_128B);
-      const uint64_t dP0 = smem_desc(smem_u32(smem + OFF_P), 16, 1024, SW_128B);
-      auto pv = [&](int m, bool first) {  // O^T += V_m^T . P_m
-        const int s = m % NS;
-        if (!wait_or(&bars->p_full[m & 1], (m >> 1) & 1, failed)) return;
-        if (!wait_or(&bars->v_full[s], (m / NS) & 1, failed)) return;
-        tc_fence_after();
-        const uint64_t dv = desc_add(dV0, s * KT), dp = desc_add(dP0, (m & 1) * 8192);
+    constexpr uint32_t idesc_s = idesc_f16(128, NH, 1, 0, 0);
+    constexpr uint32_t idesc_o = idesc_f16(128, 2 * NH, 1, 1, 0);
+    const uint64_t dK0 = smem_desc(smem_u32(smem + OFF_K), 16, 1024, SW_128B);
+    const uint64_t dV0 = smem_desc(smem_u32(smem + OFF_V), HALF, 1024, SW_128B);
+    const uint64_t dQ0 = smem_desc(smem_u32(smem + OFF_Q), 16, 1024, SW_128B);
+    const uint64_t dP0 = smem_desc(smem_u32(smem + OFF_P), 16, 1024, SW_128B);
+    const bool leader = elect_one();
+    const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
+    auto pv = [&](int m, bool first) {  // O^T += V_m^T . P_m
+      const int s = m % NS;
+      if (!wait_or(&bars->p_full[m & 1], (m >> 1) & 1, failed)) return;
+      if (!wait_or(&bars->v_full[s], (m / NS) & 1, failed)) return;
+      tc_fence_after();
+      const uint64_t dv = desc_add(dV0, s * KT), dp = desc_add(dP0, (m & 1) * 8192);
 #pragma unroll
-        for (int kk = 0; kk < TOK / 16; ++kk)
-          mma_ss(tbase + 32, desc_add(dv, kk * 16 * 128), desc_add(dp, (kk / 4) * 4096 + (kk % 4) * 32), idesc_o,
-                 (!first || kk > 0) ? 1u : 0u);
-        mma_commit(&bars->v_empty[s]);
-        mma_commit(&bars->p_free[m & 1]);
-      };
-      int n = 0, seg = 0;
-      for (int u = u_first; u <= u_last && !failed; ++u) {
-        const Unit U = unit_of(a, u, x0, x1);
-        if (U.t_hi <= U.t_lo) continue;
-        if (!wait_or(&bars->q_full, seg & 1, failed)) break;
+      for (int kk = 0; kk < TOK / 16; ++kk)
+        mma_ss(tbase + 32, desc_add(dv, kk * 16 * 128), desc_add(dp, (kk / 4) * 4096 + (kk % 4) * 32), idesc_o,
+               (!first || kk > 0) ? 1u : 0u);
+      mma_commit(&bars->v_empty[s]);
+      mma_commit(&bars->p_free[m & 1]);
+    };
+    int n = 0, seg = 0;
+    for (int k = 0; !failed; ++k) {
+      const int id = take(k, true);  // whole warp: keeps the queue walk warp-uniform
+      if (id < 0) break;
+      const Unit U = item_of(a, id, x0, x1);
+      if (U.t_hi <= U.t_lo) continue;
+      if (leader && wait_or(&bars->q_full, seg & 1, failed)) {  // no early exit here: lanes stay converged
         const int n0 = n;
         for (int ti = U.t_lo; ti < U.t_hi && !failed; ++ti, ++n) {
           const int s = n % NS;
@@ -255,8 +304,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!failed) pv(n - 1, n - 1 == n0);
         mma_commit(&bars->o_full);
-        ++seg;
       }
+      if (!leader) n += U.t_hi - U.t_lo;
+      ++seg;
+      failed = __shfl_sync(0xffffffffu, failed, leader_lane) || failed;
     }
   } else if (warp >= 2 && warp <= 5) {
     // ------------------------------------------------------------ squareplus / epilogue warps
@@ -265,8 +316,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row = 32 * quad + lane;     // token row of S^T, head-dim row of O^T
     const uint32_t tl = tbase + ((uint32_t)(32 * quad) << 16);
     const float eps4 = 4.0f * SA_EPS;
-    auto write_q = [&](int u) {
-      const Unit U = unit_of(a, u, x0, x1);
+    // Item k+1's q goes in as soon as item k's O is out of TMEM (before k's
+    // epilogue), so the MMAs of k+1 overlap the partial write / combine of k.
+    auto take_ew = [&](int k) {
+      const int id = take(k, false);
+      ew_sync();  // every epilogue thread has read the entry
+      if (e == 0 && !failed) mbar_arrive(&bars->it_empty[k % IQ]);
+      return id;
+    };
+    auto write_q = [&](const Unit& U) {
       const int r = e >> 3, j = e & 7;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -278,26 +336,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_full);
     };
-    // the first unit with work gets its q now; later ones after the previous O is read
-    auto next_busy = [&](int u) {
-      for (; u <= u_last; ++u) {
-        const Unit U = unit_of(a, u, x0, x1);
-        if (U.t_hi > U.t_lo) return u;
-      }
-      return u_last + 1;
-    };
-    int uq = next_busy(u_first);
-    if (uq <= u_last) write_q(uq);
     int n = 0, seg = 0;
-    for (int u = u_first; u <= u_last; ++u) {
-      const Unit U = unit_of(a, u, x0, x1);
+    int id = take_ew(0);
+    if (id >= 0) {
+      const Unit U0 = item_of(a, id, x0, x1);
+      if (U0.t_hi > U0.t_lo) write_q(U0);
+    }
+    for (int k = 0; id >= 0; ++k) {
+      const Unit U = item_of(a, id, x0, x1);
+      const bool busy = U.t_hi > U.t_lo;
       float ysum[NH];
 #pragma unroll
       for (int g = 0; g < NH; ++g) ysum[g] = 0.f;
       float o[NH];
 #pragma unroll
       for (int g = 0; g < NH; ++g) o[g] = 0.f;
-      const bool busy = U.t_hi > U.t_lo;
       for (int ti = U.t_lo; ti < U.t_hi; ++ti, ++n) {
         const bool ok = wait_uni(&bars->s_full[n & 1], (n >> 1) & 1, failed);
         uint32_t sr[16];
@@ -364,10 +417,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_before();
         ++seg;
       }
-      // the next busy unit's q can go in as soon as this O is out of TMEM
-      if (busy) {
-        uq = next_busy(u + 1);
-        if (uq <= u_last) write_q(uq);
+      const int id_next = take_ew(k + 1);
+      if (id_next >= 0) {
+        const Unit Un = item_of(a, id_next, x0, x1);
+        if (Un.t_hi > Un.t_lo) write_q(Un);
       }
       // sum of 4y per head over the 128 token rows of every tile
 #pragma unroll
@@ -377,7 +430,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int m = 16; m > 0; m >>= 1) ysum[g] += __shfl_xor_sync(0xffffffffu, ysum[g], m);
         }
       }
-      ew_sync();  // red[] of the previous unit fully read
+      ew_sync();  // red[] of the previous item fully read
       if (lane == 0) {
 #pragma unroll
         for (int g = 0; g < NH; ++g)
@@ -393,25 +446,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int g = 0; g < NH; ++g)
           if (g < a.GT)
             a.out[((int64_t)U.b * a.Hq + U.hq0 + g) * D + d] = __float2bfloat16_rn(o[g] / (tot[g] + eps4));
+        id = id_next;
         continue;
       }
       const int REC = a.GT * D + NH;  // o[GT][D], then up to 16 head sums
-      const int64_t ub = (int64_t)u * a.M;
-      const int64_t i0 = ((ub + 1) * NC - 1) / a.W;
-      const int64_t i1 = (min(a.W, ub + a.M) * NC - 1) / a.W;
-      float* base = a.part + (int64_t)u * a.slots * REC;
-      float* rec = base + (cta - i0) * REC;
+      float* base = a.part + (int64_t)U.u * a.slots * REC;
+      float* rec = base + (int64_t)U.slot * REC;
 #pragma unroll
       for (int g = 0; g < NH; ++g)
         if (g < a.GT) __stcg(rec + g * D + d, o[g]);
       if (e < a.GT) __stcg(rec + a.GT * D + e, red[e] + red[NH + e] + red[2 * NH + e] + red[3 * NH + e]);
       __threadfence();
       ew_sync();
-      if (e == 0) bars->last = atomicAdd(a.tickets + u, 1) == (int)(i1 - i0);
+      if (e == 0) bars->last = atomicAdd(a.tickets + U.u, 1) == U.nslots - 1;
       ew_sync();
-      if (!bars->last) continue;
+      if (!bars->last) {
+        id = id_next;
+        continue;
+      }
       __threadfence();
-      const int nsl = (int)(i1 - i0 + 1);
+      const int nsl = U.nslots;
       // Head sums: one warp, lanes stride the slots, shuffle sum (fixed order).
       if (e < 32) {
         float t[NH];
@@ -453,7 +507,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         w.y = pack2_bf16(acc.z * inv, acc.w * inv);
         *reinterpret_cast<uint2*>(a.out + ((int64_t)U.b * a.Hq + U.hq0) * D + 4 * f) = w;
       }
-      if (e == 0) a.tickets[u] = 0;  // ready for the next call
+      if (e == 0) a.tickets[U.u] = 0;  // ready for the next call
+      id = id_next;
     }
   }
 
@@ -489,9 +544,9 @@ int paged_tc_bad_pages(int reset) {
   return (int)t;
 }
 
-// Tensor-core plan: eligible shapes, grid, slots and workspace bytes.
+// Tensor-core plan: eligible shapes, schedule, slots and workspace bytes.
 bool paged_tc_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks, int64_t bs, int64_t D, int dtype,
-                   int sms, int* GT, int64_t* grid, int* slots, int64_t* ticket_bytes, int64_t* part_bytes) {
+                   int sms, PtcPlan* p) {
   if (dtype != SA_BF16 || D != ptc::D || Hq % Hkv != 0) return false;
   const int64_t G = Hq / Hkv;
   if (G < 2) return false;  // one head per KV row: the CUDA-core kernel is already HBM-bound
@@ -503,19 +558,18 @@ bool paged_tc_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_blocks, int64
   const int64_t M = (max_blocks * bs + ptc::TOK - 1) / ptc::TOK;
   if (units > INT32_MAX / 2 || M > INT32_MAX / 2) return false;
   const int64_t W = units * M;
-  *GT = gt;
-  *grid = std::max<int64_t>(1, std::min<int64_t>(sms, W));
-  const int64_t share = std::max<int64_t>(1, W / *grid);
-  *slots = (int)std::min<int64_t>(*grid, (M + share - 1) / share + 2);
-  *ticket_bytes = (units * 4 + 255) / 256 * 256;
-  *part_bytes = units * (int64_t)*slots * (gt * ptc::D + ptc::NH) * 4;
+  p->GT = gt;
+  p->grid = std::max<int64_t>(1, std::min<int64_t>(sms, W));
+  const int64_t share = std::max<int64_t>(1, W / p->grid);  // fewest tiles a non-empty CTA holds
+  p->slots = (int)std::min<int64_t>(p->grid, (M + share - 1) / share + 2);
+  p->ticket_bytes = (units * 4 + 255) / 256 * 256;
+  p->part_bytes = units * (int64_t)p->slots * (gt * ptc::D + ptc::NH) * 4;
   return true;
 }
 
 int paged_tc_launch(const void* q, const void* k_cache, const void* v_cache, void* out, const int32_t* bt,
                     const int32_t* cl, void* workspace, int64_t B, int64_t Hq, int64_t Hkv, int64_t num_blocks,
-                    int64_t bs, int64_t max_blocks, float scale, int GT, int64_t grid, int slots,
-                    int64_t ticket_bytes, cudaStream_t st) {
+                    int64_t bs, int64_t max_blocks, float scale, const PtcPlan& pl, cudaStream_t st) {
   using namespace ptc;
   CUtensorMap mk, mv;
   const int64_t strides[4] = {Hkv * bs * D, bs * D, D, 1};
@@ -527,19 +581,20 @@ int paged_tc_launch(const void* q, const void* k_cache, const void* v_cache, voi
   a.out = static_cast<__nv_bfloat16*>(out);
   a.bt = bt;
   a.cl = cl;
+  const int64_t units = B * Hkv * (Hq / Hkv / pl.GT);
   a.tickets = static_cast<int32_t*>(workspace);
-  a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ticket_bytes);
+  a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.ticket_bytes);
   a.num_blocks = num_blocks;
   a.Hq = (int)Hq;
   a.Hkv = (int)Hkv;
   a.G = (int)(Hq / Hkv);
-  a.GT = GT;
-  a.nhc = a.G / GT;
+  a.GT = pl.GT;
+  a.nhc = a.G / pl.GT;
   a.bs = (int)bs;
   a.max_blocks = (int)max_blocks;
   a.M = (int)((max_blocks * bs + TOK - 1) / TOK);
-  a.W = B * Hkv * a.nhc * (int64_t)a.M;
-  a.slots = slots;
+  a.W = units * (int64_t)a.M;
+  a.slots = pl.slots;
   a.scale2 = 2.0f * scale;
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -549,7 +604,7 @@ int paged_tc_launch(const void* q, const void* k_cache, const void* v_cache, voi
     if (e != cudaSuccess) return sa_record_cuda_error(e);
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
-  paged_tc_kernel<<<(unsigned)grid, THREADS, SMEM, st>>>(mk, mv, a);
+  paged_tc_kernel<<<(unsigned)pl.grid, THREADS, SMEM, st>>>(mk, mv, a);
   return sa_record_cuda_error(cudaGetLastError());
 }
 
