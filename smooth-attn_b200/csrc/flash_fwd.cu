@@ -128,29 +128,34 @@ __device__ __forceinline__ void kv_range(int q0, int Tq, int qoff, int Tk, int w
 template <bool BF16, bool EXACT, bool MASK>
 __device__ __forceinline__ float squareplus_regs(const uint32_t (&r)[32], uint32_t taddr_p, float scale2, int kbase,
                                                  int q, int T, int window) {
+  // Two scores per packed fp32x2 instruction: the elementwise stage, not the
+  // tensor cores, bounds this kernel, so halving its FP32 issue slots counts.
   uint32_t pk[16];
-  float sum = 0.f;
+  float2 sum = make_float2(0.f, 0.f);
+  const float2 sc2 = make_float2(scale2, scale2), m1 = make_float2(-1.0f, -1.0f), four = make_float2(4.0f, 4.0f);
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
-    float yv[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float a = fmaf(__uint_as_float(r[e + u]), scale2, -1.0f);
-      const float w = fmaf(a, a, 4.0f);
-      const float t = EXACT ? a + sqrtf(w) : fmaf(w, rsqrt_approx(w), a);
-      float y = t * t;  // 4 * squareplus(a)^2
-      if (MASK) {
-        const int k = kbase + e + u;
-        const bool ok = (k <= q) && (k < T) && (window <= 0 || q - k < window);
-        y = ok ? y : 0.f;
-      }
-      yv[u] = y;
+    const float2 a = ffma2(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, m1);
+    const float2 w = ffma2(a, a, four);
+    float2 t;
+    if (EXACT) {
+      t = make_float2(a.x + sqrtf(w.x), a.y + sqrtf(w.y));
+    } else {
+      t = ffma2(w, make_float2(rsqrt_approx(w.x), rsqrt_approx(w.y)), a);
     }
-    sum += yv[0] + yv[1];
-    pk[e / 2] = BF16 ? pack2_bf16(yv[0], yv[1]) : pack2_f16(yv[0], yv[1]);
+    float2 y = fmul2(t, t);  // 4 * squareplus(a)^2
+    if (MASK) {
+      const int k = kbase + e;
+      const bool ok0 = (k <= q) && (k < T) && (window <= 0 || q - k < window);
+      const bool ok1 = (k + 1 <= q) && (k + 1 < T) && (window <= 0 || q - k - 1 < window);
+      y.x = ok0 ? y.x : 0.f;
+      y.y = ok1 ? y.y : 0.f;
+    }
+    sum = fadd2(sum, y);
+    pk[e / 2] = BF16 ? pack2_bf16(y.x, y.y) : pack2_f16(y.x, y.y);
   }
   tmem_st16(taddr_p, pk);
-  return sum;
+  return sum.x + sum.y;
 }
 
 // One 128-column score row: TMEM loads run one chunk ahead of the math
