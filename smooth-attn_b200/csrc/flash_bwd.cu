@@ -460,7 +460,7 @@ __device__ __forceinline__ bool ew_all(bool v) {
 }
 
 // Per query column m the loader stores c4[m] = 1/(4R), cs[m] = scale/R and
-// cd[m] = delta*scale/R, so with t = a + sqrt(a^2+4) = 2 sp and
+// -cd[m] = -delta*scale/R, so with t = a + sqrt(a^2+4) = 2 sp and
 // h = 1 + a rsqrt(a^2+4) = 2 sp':
 //   P  = sp^2 / R                      = t*t*c4
 //   dS = (dP - delta)/R * 4 sp sp' s   = (dP*cs - cd) * t*h
@@ -482,29 +482,39 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
     for (int e = 0; e < 16; e += 4) {
       const float4 c4v = *reinterpret_cast<const float4*>(vec + col + e);
       const float4 csv = *reinterpret_cast<const float4*>(vec + 64 + col + e);
-      const float4 cdv = *reinterpret_cast<const float4*>(vec + 128 + col + e);
-      const float c4[4] = {c4v.x, c4v.y, c4v.z, c4v.w};
-      const float cs[4] = {csv.x, csv.y, csv.z, csv.w};
-      const float cd[4] = {cdv.x, cdv.y, cdv.z, cdv.w};
+      const float4 cdv = *reinterpret_cast<const float4*>(vec + 128 + col + e);  // -cd
+      const float2 c4p[2] = {make_float2(c4v.x, c4v.y), make_float2(c4v.z, c4v.w)};
+      const float2 csp[2] = {make_float2(csv.x, csv.y), make_float2(csv.z, csv.w)};
+      const float2 cdp[2] = {make_float2(cdv.x, cdv.y), make_float2(cdv.z, cdv.w)};
       float pv[4], dsv[4];
+      // two query columns per packed fp32x2 instruction (bit-identical to the
+      // scalar ops; the elementwise stage bounds this kernel's issue slots)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 4; u += 2) {
         const int idx = 16 * hf + e + u;
-        const float a = fmaf(__uint_as_float(sv[idx]), scale2, -1.0f);
-        const float w = fmaf(a, a, 4.0f);
-        const float rs = rsqrt_approx(w);
-        const float t = EXACT ? a + sqrtf(w) : fmaf(w, rs, a);
-        const float hh = fmaf(a, rs, 1.0f);
-        float pp = t * t * c4[u];
-        float ds = fmaf(__uint_as_float(dv[idx]), cs[u], -cd[u]) * (t * hh);
+        const float2 a = ffma2(make_float2(__uint_as_float(sv[idx]), __uint_as_float(sv[idx + 1])),
+                               make_float2(scale2, scale2), make_float2(-1.0f, -1.0f));
+        const float2 w = ffma2(a, a, make_float2(4.0f, 4.0f));
+        const float2 rs = make_float2(rsqrt_approx(w.x), rsqrt_approx(w.y));
+        const float2 t = EXACT ? make_float2(a.x + sqrtf(w.x), a.y + sqrtf(w.y)) : ffma2(w, rs, a);
+        const float2 hh = ffma2(a, rs, make_float2(1.0f, 1.0f));
+        float2 pp = fmul2(fmul2(t, t), c4p[u / 2]);
+        float2 ds = fmul2(ffma2(make_float2(__uint_as_float(dv[idx]), __uint_as_float(dv[idx + 1])), csp[u / 2],
+                                cdp[u / 2]),
+                          fmul2(t, hh));
         if (MASK) {
           const int q = q0 + col + e + u;
-          const bool ok = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
-          pp = ok ? pp : 0.f;
-          ds = ok ? ds : 0.f;
+          const bool ok0 = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
+          const bool ok1 = (n <= q + 1) && (q + 1 < T) && (n < T) && (window <= 0 || q + 1 - n < window);
+          pp.x = ok0 ? pp.x : 0.f;
+          ds.x = ok0 ? ds.x : 0.f;
+          pp.y = ok1 ? pp.y : 0.f;
+          ds.y = ok1 ? ds.y : 0.f;
         }
-        pv[u] = pp;
-        dsv[u] = ds;
+        pv[u] = pp.x;
+        pv[u + 1] = pp.y;
+        dsv[u] = ds.x;
+        dsv[u + 1] = ds.y;
       }
       pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
       pk[e / 2 + 1] = BF16 ? pack2_bf16(pv[2], pv[3]) : pack2_f16(pv[2], pv[3]);
@@ -768,7 +778,7 @@ __global__ void __launch_bounds__(448, 1)
         float* vb = vVec + bb * 192;
         vb[tid] = 0.25f * ir;
         vb[64 + tid] = p.scale * ir;
-        vb[128 + tid] = pre_d * p.scale * ir;
+        vb[128 + tid] = -(pre_d * p.scale * ir);  // stored negated: dP*cs - cd is one fma
       }
       ew_sync();
       prefetch(it + 1);
