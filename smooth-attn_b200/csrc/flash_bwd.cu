@@ -843,29 +843,52 @@ __global__ void __launch_bounds__(256) flash_bwd_prep(const T* __restrict__ o, c
                                                       float* __restrict__ delta, float* __restrict__ dq_acc,
                                                       int64_t rows, int Hq, int Tlen, int64_t so_b, int64_t so_h,
                                                       int64_t so_s, int64_t sd_b, int64_t sd_h, int64_t sd_s) {
+  // delta = rowsum(dO * O) and a zeroed fp32 dQ accumulator.  LPR lanes per
+  // row (16 bytes each of O and dO); two rows per lane group per pass so four
+  // 16-byte loads are in flight per thread; grid-stride over the rows.
   constexpr int VEC = 8;  // 16 bytes of 16-bit elements
-  constexpr int NV = D / VEC;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const int t = (int)(row % Tlen);
-  const int64_t bh = row / Tlen;
-  const int b = (int)(bh / Hq), h = (int)(bh % Hq);
-  const T* orow = o + (int64_t)b * so_b + (int64_t)h * so_h + (int64_t)t * so_s;
-  const T* drow = dout + (int64_t)b * sd_b + (int64_t)h * sd_h + (int64_t)t * sd_s;
-  float acc = 0.f;
-  if (lane < NV) {
-    Pack<T, VEC> a, c;
-    a.u = *reinterpret_cast<const uint4*>(orow + lane * VEC);
-    c.u = *reinterpret_cast<const uint4*>(drow + lane * VEC);
+  constexpr int LPR = D / VEC;
+  constexpr int RPB = 256 / LPR;  // rows per block per pass
+  const int sub = threadIdx.x % LPR;
+  const int64_t stride = (int64_t)gridDim.x * RPB;
+  auto addr = [&](int64_t row, const T* base, int64_t sb, int64_t sh, int64_t ss) {
+    const int t = (int)(row % Tlen);
+    const int64_t bh = row / Tlen;
+    return base + (bh / Hq) * sb + (bh % Hq) * sh + (int64_t)t * ss + sub * VEC;
+  };
+  for (int64_t r0 = (int64_t)blockIdx.x * RPB + threadIdx.x / LPR; r0 < rows; r0 += 2 * stride) {
+    const int64_t r1 = r0 + stride;
+    const bool two = r1 < rows;
+    Pack<T, VEC> a0, c0, a1, c1;
+    a0.u = *reinterpret_cast<const uint4*>(addr(r0, o, so_b, so_h, so_s));
+    c0.u = *reinterpret_cast<const uint4*>(addr(r0, dout, sd_b, sd_h, sd_s));
+    if (two) {
+      a1.u = *reinterpret_cast<const uint4*>(addr(r1, o, so_b, so_h, so_s));
+      c1.u = *reinterpret_cast<const uint4*>(addr(r1, dout, sd_b, sd_h, sd_s));
+    }
+    float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) acc += a.get(e) * c.get(e);
+    for (int e = 0; e < VEC; ++e) acc0 += a0.get(e) * c0.get(e);
+    if (two) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc1 += a1.get(e) * c1.get(e);
+    }
+#pragma unroll
+    for (int off = LPR / 2; off > 0; off >>= 1) {
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, off);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, off);
+    }
+    if (sub == 0) {
+      delta[r0] = acc0;
+      if (two) delta[r1] = acc1;
+    }
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = sub; i < D / 4; i += LPR) {
+      reinterpret_cast<float4*>(dq_acc + r0 * D)[i] = z;
+      if (two) reinterpret_cast<float4*>(dq_acc + r1 * D)[i] = z;
+    }
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) delta[row] = acc;
-  float4* z = reinterpret_cast<float4*>(dq_acc + row * D);
-  for (int i = lane; i < D / 4; i += 32) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 template <typename T, int D>
@@ -898,7 +921,13 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
   using C = BwdCfg<D>;
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int64_t rows = B * Hq * T;
-  flash_bwd_prep<T16, D><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+  int prep_dev = 0, prep_sms = 148;
+  if (cudaGetDevice(&prep_dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&prep_sms, cudaDevAttrMultiProcessorCount, prep_dev);
+  const int64_t prep_rpb = 256 / (D / 8);
+  flash_bwd_prep<T16, D><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + prep_rpb - 1) / prep_rpb,
+                                                                              (int64_t)prep_sms * 8)),
+                           256, 0, st>>>(
       static_cast<const T16*>(o), static_cast<const T16*>(dout), delta, dq_acc, rows, (int)Hq, (int)T, os[0], os[1],
       os[2], dos[0], dos[1], dos[2]);
   CUtensorMap mq, mk, mv, mdo;
@@ -1037,6 +1066,7 @@ extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const v
 
 static __device__ __align__(256) unsigned char g_bwd_noalloc_scratch[SA_NOALLOC_SCRATCH_BYTES];
 
+#include <algorithm>
 #include <mutex>
 
 // Device address of the scratch array for the current device.  In host code
