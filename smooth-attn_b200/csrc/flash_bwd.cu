@@ -90,32 +90,34 @@ __device__ __forceinline__ void bwd_chunk(uint32_t tl, int c, uint8_t* sDS, int 
   tmem_ld32(tl + 128 + c * 32, dv);
   tmem_ld_wait();
   uint32_t pk[16], dk[16];
+  const float2 half = make_float2(0.5f, 0.5f), c4s2 = make_float2(c4s, c4s);
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
-    float pv[2], dsv[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int m = c * 32 + e + u;
-      const float a = fmaf(__uint_as_float(sv[e + u]), scale2, -1.0f);
-      const float w = fmaf(a, a, 4.0f);
-      const float rs = rsqrt_approx(w);
-      const float sq = EXACT ? sqrtf(w) : w * rs;
-      const float sp = 0.5f * (a + sq);
-      const float spp = 0.5f * fmaf(a, rs, 1.0f);
-      const float invR = sInvR[m];
-      float pp = sp * sp * invR;
-      float ds = (__uint_as_float(dv[e + u]) - sDelta[m]) * invR * (c4s * sp * spp);
-      if (MASK) {
-        const int q = q0 + m;
-        const bool ok = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
-        pp = ok ? pp : 0.f;
-        ds = ok ? ds : 0.f;
-      }
-      pv[u] = pp;
-      dsv[u] = ds;
+    // two query columns per packed fp32x2 instruction (bit-identical to scalar)
+    const int m = c * 32 + e;
+    const float2 a = ffma2(make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])),
+                           make_float2(scale2, scale2), make_float2(-1.0f, -1.0f));
+    const float2 w = ffma2(a, a, make_float2(4.0f, 4.0f));
+    const float2 rs = make_float2(rsqrt_approx(w.x), rsqrt_approx(w.y));
+    const float2 sq = EXACT ? make_float2(sqrtf(w.x), sqrtf(w.y)) : fmul2(w, rs);
+    const float2 sp = fmul2(half, fadd2(a, sq));
+    const float2 spp = fmul2(half, ffma2(a, rs, make_float2(1.0f, 1.0f)));
+    const float2 invR = *reinterpret_cast<const float2*>(sInvR + m);
+    const float2 dl = *reinterpret_cast<const float2*>(sDelta + m);
+    float2 pp = fmul2(fmul2(sp, sp), invR);
+    float2 ds = fmul2(fmul2(fsub2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), dl), invR),
+                      fmul2(fmul2(c4s2, sp), spp));
+    if (MASK) {
+      const int q = q0 + m;
+      const bool ok0 = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
+      const bool ok1 = (n <= q + 1) && (q + 1 < T) && (n < T) && (window <= 0 || q + 1 - n < window);
+      pp.x = ok0 ? pp.x : 0.f;
+      ds.x = ok0 ? ds.x : 0.f;
+      pp.y = ok1 ? pp.y : 0.f;
+      ds.y = ok1 ? ds.y : 0.f;
     }
-    pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
-    dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
+    pk[e / 2] = BF16 ? pack2_bf16(pp.x, pp.y) : pack2_f16(pp.x, pp.y);
+    dk[e / 2] = BF16 ? pack2_bf16(ds.x, ds.y) : pack2_f16(ds.x, ds.y);
   }
   tmem_st16(tl + c * 16, pk);
   uint8_t* row = sDS + (c >> 1) * (128 * 128) + r * 128;
