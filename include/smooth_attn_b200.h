@@ -190,6 +190,24 @@ SA_API int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void*
                               int dtype, void* stream);
 
 /*
+ * Backward of sa_flash_fwd_chunk: gradients of a block of Tq queries at
+ * global positions q_offset .. against keys / values 0 .. Tk-1.  dq:
+ * [B, Hq, Tq, D] (complete for these queries); dk, dv: [B, Hkv, Tk, D] hold
+ * this query block's contribution only (a context-parallel caller adds the
+ * contributions of every rank's query blocks).  rowsum / o from the chunk
+ * forward; workspace: sa_flash_bwd_workspace_size(B, Hq, Hkv, Tq, D) bytes.
+ * Other arguments as sa_flash_bwd (which is this call with Tq = Tk = T,
+ * q_offset = 0).  (No reference counterpart.)
+ */
+SA_API int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                              const float* rowsum, void* dq, void* dk, void* dv, void* workspace,
+                              int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk,
+                              int64_t q_offset, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+                              const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                              float scale, int64_t window_size, int exact_math, int dtype, void* stream);
+
+/*
  * Rotary position embedding, rotate-half form, rounded to the input type:
  *   out[..., i] = x1 c - x2 s,  out[..., i + D/2] = x2 c + x1 s
  * with x1 = x[..., i], x2 = x[..., i + D/2], c = cos[t, i], s = sin[t, i],

@@ -268,6 +268,49 @@ def sp2norm_flash_attention_bwd(q, k, v, do, scale=None, window_size=0, acc=np.f
     return dq, dk, dv
 
 
+def chunk_flash_attention_bwd(q, k, v, do, q_offset, scale=None, window_size=0, acc=np.float32):
+    """Gradients of ``sum(chunk_flash_attention(q, k, v, q_offset) * do)``:
+    dq for the query block, dk / dv for keys 0 .. Tk-1 (this block's
+    contribution).  Same closed form as sp2norm_flash_attention_bwd with the
+    mask in global positions."""
+    q = _as_f(q, acc)
+    k_in = _as_f(k, acc)
+    v_in = _as_f(v, acc)
+    do = _as_f(do, acc)
+    B, Hq, Tq, D = q.shape
+    Hkv, Tk = k_in.shape[1], k_in.shape[2]
+    k = _expand_kv(k_in, Hq)
+    v = _expand_kv(v_in, Hq)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    qp = np.arange(Tq)[:, None] + q_offset
+    kp = np.arange(Tk)[None, :]
+    mask = kp <= qp
+    if window_size > 0:
+        mask &= (qp - kp) < window_size
+    s = np.matmul(q, np.swapaxes(k, -1, -2)) * acc(scale)
+    a = acc(2.0) * s - acc(1.0)
+    rt = np.sqrt(a * a + acc(4.0))
+    sp = acc(0.5) * (a + rt)
+    spp = acc(0.5) * (acc(1.0) + a / rt)
+    y = np.where(mask, sp * sp, acc(0.0))
+    r = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    p = y / r
+    o = np.matmul(p, v)
+    delta = (do * o).sum(axis=-1, keepdims=True)
+    dp = np.matmul(do, np.swapaxes(v, -1, -2))
+    dy = np.where(mask, (dp - delta) / r, acc(0.0))
+    ds = dy * acc(4.0) * sp * spp * acc(scale)
+    dq = np.matmul(ds, k)
+    dk = np.matmul(np.swapaxes(ds, -1, -2), q)
+    dv = np.matmul(np.swapaxes(p, -1, -2), do)
+    if Hkv != Hq:
+        g = Hq // Hkv
+        dk = dk.reshape(B, Hkv, g, Tk, D).sum(axis=2)
+        dv = dv.reshape(B, Hkv, g, Tk, D).sum(axis=2)
+    return dq, dk, dv
+
+
 def paged_decode_attention(q, k_cache, v_cache, block_table, context_lens, scale=None, acc=np.float32):
     """Decode attention over a paged KV cache (kernels.py:2681-2829 and the
     reference's decode reference, tests/test_paged_attention.py:78-109).

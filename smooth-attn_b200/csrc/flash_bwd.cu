@@ -83,8 +83,8 @@ __device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 128;"
 // dS -> the swizzled shared-memory tile.
 template <bool BF16, bool EXACT, bool MASK>
 __device__ __forceinline__ void bwd_chunk(uint32_t tl, int c, uint8_t* sDS, int r, const float* sInvR,
-                                          const float* sDelta, float scale2, float c4s, int n, int q0, int T,
-                                          int window) {
+                                          const float* sDelta, float scale2, float c4s, int n, int q0, int qend,
+                                          int Tk, int window) {
   uint32_t sv[32], dv[32];
   tmem_ld32(tl + c * 32, sv);
   tmem_ld32(tl + 128 + c * 32, dv);
@@ -108,9 +108,9 @@ __device__ __forceinline__ void bwd_chunk(uint32_t tl, int c, uint8_t* sDS, int 
     float2 ds = fmul2(fmul2(fsub2(make_float2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), dl), invR),
                       fmul2(fmul2(c4s2, sp), spp));
     if (MASK) {
-      const int q = q0 + m;
-      const bool ok0 = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
-      const bool ok1 = (n <= q + 1) && (q + 1 < T) && (n < T) && (window <= 0 || q + 1 - n < window);
+      const int q = q0 + m;  // global query position (q0 global); qend = one past the last query
+      const bool ok0 = (n <= q) && (q < qend) && (n < Tk) && (window <= 0 || q - n < window);
+      const bool ok1 = (n <= q + 1) && (q + 1 < qend) && (n < Tk) && (window <= 0 || q + 1 - n < window);
       pp.x = ok0 ? pp.x : 0.f;
       ds.x = ok0 ? ds.x : 0.f;
       pp.y = ok1 ? pp.y : 0.f;
@@ -157,9 +157,39 @@ struct BwdParams {
   float* dq_acc;        // [B, Hq, T, D] fp32
   int64_t sdk_b, sdk_h, sdk_s;
   int64_t sdv_b, sdv_h, sdv_s;
-  int B, Hq, Hkv, T, window;
+  int B, Hq, Hkv, T, window;  // T: query rows
+  int Tk, qoff;                 // key rows; global position of query row 0 (keys start at 0)
   float scale;
 };
+
+// Query tiles [qt_first, qt_last] (local, BQ rows each) that see some key of
+// the KV tile [n0, n0 + BN): query rows at global positions >= n0 and, with a
+// window, < n0 + BN - 1 + window.  Empty when qt_last < qt_first.
+__device__ __forceinline__ void query_tile_range(const BwdParams& p, int n0, int BN, int BQ, int& qt_first,
+                                                 int& qt_last) {
+  const int first_local = n0 - p.qoff;
+  qt_first = first_local > 0 ? first_local / BQ : 0;
+  qt_last = (p.T + BQ - 1) / BQ - 1;
+  if (p.window > 0) {
+    const int last_local = n0 + BN - 1 + p.window - 1 - p.qoff;
+    const int l = last_local >= 0 ? last_local / BQ : -1;
+    if (l < qt_last) qt_last = l;
+  }
+}
+
+template <int D, int BN>
+__device__ void zero_dkdv(const BwdParams& p, int b, int kvh, int n0) {
+  for (int i = threadIdx.x; i < 2 * BN * (D / 8); i += blockDim.x) {
+    const int which = i / (BN * (D / 8));
+    const int rem = i - which * BN * (D / 8);
+    const int n = n0 + rem / (D / 8), c = rem % (D / 8);
+    if (n >= p.Tk) continue;
+    uint8_t* base = static_cast<uint8_t*>(which ? p.dv : p.dk) +
+                    2 * (which ? ((int64_t)b * p.sdv_b + (int64_t)kvh * p.sdv_h + (int64_t)n * p.sdv_s)
+                               : ((int64_t)b * p.sdk_b + (int64_t)kvh * p.sdk_h + (int64_t)n * p.sdk_s));
+    reinterpret_cast<uint4*>(base)[c] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
 
 struct BwdBars {
   uint64_t kv_full;
@@ -194,16 +224,14 @@ __global__ void __launch_bounds__(192, 1)
   const int n0 = blockIdx.x * C::BN;
   const int b = blockIdx.y / p.Hkv, kvh = blockIdx.y % p.Hkv;
   const int G = p.Hq / p.Hkv;
-  const int nqt = (p.T + C::BQ - 1) / C::BQ;
-  const int qt_first = n0 / C::BQ;
-  int qt_last = nqt - 1;
-  if (p.window > 0) {
-    const int last_q = n0 + C::BN - 1 + p.window - 1;
-    const int l = last_q / C::BQ;
-    if (l < qt_last) qt_last = l;
-  }
+  int qt_first, qt_last;
+  query_tile_range(p, n0, C::BN, C::BQ, qt_first, qt_last);
   const int per_head = qt_last - qt_first + 1;
-  const int ntiles = G * per_head;
+  const int ntiles = per_head > 0 ? G * per_head : 0;
+  if (ntiles == 0) {  // no query sees these keys: dK = dV = 0 (before any barrier)
+    zero_dkdv<D, C::BN>(p, b, kvh, n0);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->kv_full, 1);
@@ -334,16 +362,17 @@ __global__ void __launch_bounds__(192, 1)
       prefetch(it + 1);
       if (!b_warp_wait(&bars->s_full, it & 1, failed)) break;
       tc_fence_after();
-      const bool need_mask = (q0 < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.T) ||
-                             (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
+      const int q0g = q0 + p.qoff, qend = p.qoff + p.T;  // global query positions
+      const bool need_mask = (q0g < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.Tk) ||
+                             (p.window > 0 && q0g + C::BQ - 1 - n0 >= p.window);
       if (need_mask) {
 #pragma unroll 1
         for (int c = 0; c < C::BQ / 32; ++c)
-          bwd_chunk<BF16, EXACT, true>(tl, c, sDS, r, sInvR, sDelta, scale2, c4s, n, q0, p.T, p.window);
+          bwd_chunk<BF16, EXACT, true>(tl, c, sDS, r, sInvR, sDelta, scale2, c4s, n, q0g, qend, p.Tk, p.window);
       } else {
 #pragma unroll 1
         for (int c = 0; c < C::BQ / 32; ++c)
-          bwd_chunk<BF16, EXACT, false>(tl, c, sDS, r, sInvR, sDelta, scale2, c4s, n, q0, p.T, p.window);
+          bwd_chunk<BF16, EXACT, false>(tl, c, sDS, r, sInvR, sDelta, scale2, c4s, n, q0g, qend, p.Tk, p.window);
       }
       tmem_st_wait();
       fence_proxy_async_smem();
@@ -372,7 +401,7 @@ __global__ void __launch_bounds__(192, 1)
     // epilogue: dK, dV rows (TMEM lane = KV row)
     if (b_warp_wait(&bars->all_done, 0, failed)) {
       tc_fence_after();
-      const bool live = n < p.T;
+      const bool live = n < p.Tk;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         uint8_t* base = static_cast<uint8_t*>(which ? p.dv : p.dk) +
@@ -470,7 +499,8 @@ __device__ __forceinline__ bool ew_all(bool v) {
 // packed and stored 16 columns at a time to keep register use low.
 template <bool BF16, bool EXACT, bool MASK>
 __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, uint8_t* dsrow, int r,
-                                             const float* vec, float scale2, int n, int q0, int T, int window) {
+                                             const float* vec, float scale2, int n, int q0, int qend, int Tk,
+                                             int window) {
   uint32_t sv[32], dv[32];
   tmem_ld32(tS + 32 * w2, sv);
   tmem_ld32(tP + 32 * w2, dv);
@@ -505,9 +535,9 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
                                 cdp[u / 2]),
                           fmul2(t, hh));
         if (MASK) {
-          const int q = q0 + col + e + u;
-          const bool ok0 = (n <= q) && (q < T) && (n < T) && (window <= 0 || q - n < window);
-          const bool ok1 = (n <= q + 1) && (q + 1 < T) && (n < T) && (window <= 0 || q + 1 - n < window);
+          const int q = q0 + col + e + u;  // global query position
+          const bool ok0 = (n <= q) && (q < qend) && (n < Tk) && (window <= 0 || q - n < window);
+          const bool ok1 = (n <= q + 1) && (q + 1 < qend) && (n < Tk) && (window <= 0 || q + 1 - n < window);
           pp.x = ok0 ? pp.x : 0.f;
           ds.x = ok0 ? ds.x : 0.f;
           pp.y = ok1 ? pp.y : 0.f;
@@ -555,15 +585,14 @@ __global__ void __launch_bounds__(448, 1)
   const int n0 = blockIdx.x * C::BN;
   const int b = blockIdx.y / p.Hkv, kvh = blockIdx.y % p.Hkv;
   const int G = p.Hq / p.Hkv;
-  const int nqt = (p.T + C::BQ - 1) / C::BQ;
-  const int qt_first = n0 / C::BQ;
-  int qt_last = nqt - 1;
-  if (p.window > 0) {
-    const int l = (n0 + C::BN - 1 + p.window - 1) / C::BQ;
-    if (l < qt_last) qt_last = l;
-  }
+  int qt_first, qt_last;
+  query_tile_range(p, n0, C::BN, C::BQ, qt_first, qt_last);
   const int per_head = qt_last - qt_first + 1;
-  const int ntiles = G * per_head;
+  const int ntiles = per_head > 0 ? G * per_head : 0;
+  if (ntiles == 0) {  // no query sees these keys: dK = dV = 0 (before any barrier)
+    zero_dkdv<D, C::BN>(p, b, kvh, n0);
+    return;
+  }
   // Tiles run head-major: (head kvh*G + g, query tile qt_first .. qt_last).
   // Each role walks them with an incremental cursor (no integer division).
   struct Cursor {
@@ -791,15 +820,16 @@ __global__ void __launch_bounds__(448, 1)
         break;
       }
       tc_fence_after();
-      const bool need_mask = (q0 < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.T) ||
-                             (p.window > 0 && q0 + C::BQ - 1 - n0 >= p.window);
+      const int q0g = q0 + p.qoff, qend = p.qoff + p.T;  // global query positions
+      const bool need_mask = (q0g < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.Tk) ||
+                             (p.window > 0 && q0g + C::BQ - 1 - n0 >= p.window);
       uint8_t* dsrow = sDS + bb * C::DS_TILE + r * 128;
       if (need_mask)
         bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vVec + bb * 192, scale2,
-                                        n, q0, p.T, p.window);
+                                        n, q0g, qend, p.Tk, p.window);
       else
         bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vVec + bb * 192, scale2,
-                                         n, q0, p.T, p.window);
+                                         n, q0g, qend, p.Tk, p.window);
       tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
@@ -808,7 +838,7 @@ __global__ void __launch_bounds__(448, 1)
     // epilogue: warpgroup 0 writes dK, warpgroup 1 writes dV (TMEM lane = KV row)
     if (b_warp_wait(&bars->all_done, 0, failed)) {
       tc_fence_after();
-      const bool live = n < p.T;
+      const bool live = n < p.Tk;
       uint8_t* base = static_cast<uint8_t*>(w2 ? p.dv : p.dk) +
                       2 * (w2 ? ((int64_t)b * p.sdv_b + (int64_t)kvh * p.sdv_h + (int64_t)n * p.sdv_s)
                               : ((int64_t)b * p.sdk_b + (int64_t)kvh * p.sdk_h + (int64_t)n * p.sdk_s));
@@ -919,8 +949,10 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
                       const float* rowsum, void* dq, void* dk, void* dv, float* dq_acc, float* delta, int64_t B,
                       int64_t Hq, int64_t Hkv, int64_t T, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                       const int64_t* os, const int64_t* dos, const int64_t* dqs, const int64_t* dks,
-                      const int64_t* dvs, float scale, int64_t window, cudaStream_t st) {
+                      const int64_t* dvs, float scale, int64_t window, cudaStream_t st, int64_t Tk = -1,
+                      int64_t qoff = 0) {
   using C = BwdCfg<D>;
+  if (Tk < 0) Tk = T;
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int64_t rows = B * Hq * T;
   int prep_dev = 0, prep_sms = 148;
@@ -934,8 +966,8 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
       os[2], dos[0], dos[1], dos[2]);
   CUtensorMap mq, mk, mv, mdo;
   if (!make_map_4d(&mq, q, BF16, B, Hq, T, D, qs, C::CHUNK, C::BQ) ||
-      !make_map_4d(&mk, k, BF16, B, Hkv, T, D, ks, C::CHUNK, C::BN) ||
-      !make_map_4d(&mv, v, BF16, B, Hkv, T, D, vs, C::CHUNK, C::BN) ||
+      !make_map_4d(&mk, k, BF16, B, Hkv, Tk, D, ks, C::CHUNK, C::BN) ||
+      !make_map_4d(&mv, v, BF16, B, Hkv, Tk, D, vs, C::CHUNK, C::BN) ||
       !make_map_4d(&mdo, dout, BF16, B, Hq, T, D, dos, C::CHUNK, C::BQ))
     return SA_ERR_ALIGN;
   BwdParams p;
@@ -950,9 +982,11 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
   p.Hq = (int)Hq;
   p.Hkv = (int)Hkv;
   p.T = (int)T;
+  p.Tk = (int)Tk;
+  p.qoff = (int)qoff;
   p.window = (int)window;
   p.scale = scale;
-  dim3 grid((unsigned)((T + C::BN - 1) / C::BN), (unsigned)(B * Hkv));
+  dim3 grid((unsigned)((Tk + C::BN - 1) / C::BN), (unsigned)(B * Hkv));
   if constexpr (D == 128) {
     CUtensorMap mq64, mdo64;
     if (!make_map_4d(&mq64, q, BF16, B, Hq, T, D, qs, 64, Bwd128::BQ) ||
@@ -1048,6 +1082,58 @@ extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const v
   }
 #undef SA_BWD_D
 #undef SA_BWD_CASE
+  if (rc != SA_OK) return rc;
+  return sa_record_cuda_error(cudaGetLastError());
+}
+
+extern "C" int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                  const float* rowsum, void* dq, void* dk, void* dv, void* workspace,
+                                  int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk,
+                                  int64_t q_offset, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
+                                  const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
+                                  const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
+                                  float scale, int64_t window_size, int exact_math, int dtype, void* stream) {
+  if (dtype != SA_BF16 && dtype != SA_F16) return SA_ERR_UNSUPPORTED;
+  if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
+  if (B < 0 || Hq < 1 || Hkv < 1 || Tq < 0 || Tk < 0 || q_offset < 0 || Hq % Hkv != 0 || window_size < 0)
+    return SA_ERR_ARG;
+  if (B == 0 || Tq == 0 || Tk == 0) return Tk == 0 && Tq > 0 ? SA_ERR_ARG : SA_OK;
+  if (Tq > (1ll << 30) || Tk > (1ll << 30) || q_offset > (1ll << 30) || B * Hkv > 65535) return SA_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !o || !dout || !rowsum || !dq || !dk || !dv || !workspace) return SA_ERR_ARG;
+  if (workspace_bytes < sa_flash_bwd_workspace_size(B, Hq, Hkv, Tq, D)) return SA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_ALIGN;
+  const int64_t* all[8] = {q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides};
+  for (auto s : all)
+    if (!bwd_strides_ok(s)) return SA_ERR_ALIGN;
+  const void* ptrs[9] = {q, k, v, o, dout, dq, dk, dv, rowsum};
+  for (auto p : ptrs)
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return SA_ERR_ALIGN;
+  float* dq_acc = static_cast<float*>(workspace);
+  float* delta = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(B * Hq * Tq * D * 4));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  using namespace sa::flash;
+  int rc;
+#define SA_BWDC_CASE(DD, BF, EX)                                                                                 \
+  rc = launch_bwd<DD, BF, EX>(q, k, v, o, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, Tq, q_strides,   \
+                              k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, \
+                              scale, window_size, st, Tk, q_offset)
+#define SA_BWDC_D(DD)                              \
+  if (dtype == SA_BF16) {                          \
+    if (exact_math) SA_BWDC_CASE(DD, true, true);  \
+    else SA_BWDC_CASE(DD, true, false);            \
+  } else {                                         \
+    if (exact_math) SA_BWDC_CASE(DD, false, true); \
+    else SA_BWDC_CASE(DD, false, false);           \
+  }
+  if (D == 32) {
+    SA_BWDC_D(32)
+  } else if (D == 64) {
+    SA_BWDC_D(64)
+  } else {
+    SA_BWDC_D(128)
+  }
+#undef SA_BWDC_D
+#undef SA_BWDC_CASE
   if (rc != SA_OK) return rc;
   return sa_record_cuda_error(cudaGetLastError());
 }

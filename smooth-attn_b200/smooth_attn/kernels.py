@@ -543,6 +543,40 @@ def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=
     return o, row_sums
 
 
+def sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, row_sums, q_offset, *, scale=None, window_size=0,
+                                      exact_math=False):
+    """Backward of ``sp2norm_flash_attention_chunk`` (``sa_flash_bwd_chunk``).
+
+    Returns (dq [B, H_q, Tq, D], dk, dv [B, H_kv, Tk, D]): dq is complete for
+    the query block; dk / dv hold this block's contribution only (the
+    context-parallel backward sums them over every rank's query blocks).
+    """
+    B, H_q, Tq, D = q.shape
+    H_kv, Tk = k.shape[1], k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    q, k, v, o, do = (_flash_ready(t) for t in (q, k, v, o, do))
+    dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    dk = torch.empty(k.shape, device=q.device, dtype=q.dtype)
+    dv = torch.empty(v.shape, device=q.device, dtype=q.dtype)
+    if q.numel() == 0:
+        return dq, dk.zero_(), dv.zero_()
+    lib = _lib.load()
+    ws_bytes = int(lib.sa_flash_bwd_workspace_size(B, H_q, H_kv, Tq, D))
+    ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
+    with torch.cuda.device(q.device):
+        st = lib.sa_flash_bwd_chunk(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), row_sums.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
+            B, H_q, H_kv, Tq, Tk, int(q_offset), D,
+            _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o), _lib.strides(do),
+            _lib.strides(dq), _lib.strides(dk), _lib.strides(dv),
+            float(scale), int(window_size), int(bool(exact_math)), _DTYPE_CODE[q.dtype], _stream(q),
+        )
+    _lib.check(st, "sa_flash_bwd_chunk")
+    return dq, dk, dv
+
+
 # ---------------------------------------------------------------------------
 # forward-only extensions outside this build's hot path (kernels.py:2093-2829)
 # ---------------------------------------------------------------------------

@@ -128,34 +128,99 @@ def _all_gather(x: torch.Tensor, group=None) -> list:
     return parts
 
 
+def _reduce_scatter_zigzag(full: torch.Tensor, group=None, dim: int = 2) -> torch.Tensor:
+    """Sum ``full`` (this rank's contribution over the whole sequence, in
+    sequence order) over ranks and return this rank's two zig-zag chunks."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    chunks = full.chunk(2 * world, dim=dim)
+    blocks = [torch.cat([chunks[a], chunks[b]], dim=dim) for a, b in (zigzag_chunk_ids(world, r) for r in range(world))]
+    if dist.get_backend(group) == "nccl":
+        inp = torch.stack(blocks).contiguous()
+        out = torch.empty_like(blocks[0])
+        dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.SUM, group=group)
+        return out
+    total = torch.stack(blocks).contiguous()  # gloo has no reduce_scatter: all-reduce, keep own block
+    dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group)
+    return total[rank].clone()
+
+
+def _cp_gather_kv(k, v, group):
+    kv = torch.stack([k, v]).contiguous()
+    return zigzag_merge(_all_gather(kv, group), dim=3)  # [2, B, Hkv, T, D] in sequence order
+
+
+class _ContextParallelAttnFn(torch.autograd.Function):
+    """Forward: all-gather K/V, chunk forwards.  Backward: all-gather K/V again,
+    chunk backwards (dQ complete per local chunk, dK/dV contributions over the
+    visible key prefix), then a reduce-scatter sums the dK/dV contributions of
+    every rank into their owners' zig-zag chunks."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, group, scale, window_size):
+        from . import kernels
+
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        C = q.shape[2] // 2
+        full = _cp_gather_kv(k, v, group)
+        outs, sums = [], []
+        for i, c in enumerate(zigzag_chunk_ids(world, rank)):
+            qc = q[:, :, i * C:(i + 1) * C]
+            o, r = kernels.sp2norm_flash_attention_chunk(qc, full[0, :, :, :(c + 1) * C], full[1, :, :, :(c + 1) * C],
+                                                         c * C, scale=scale, window_size=window_size)
+            outs.append(o)
+            sums.append(r)
+        o = torch.cat(outs, dim=2)
+        ctx.save_for_backward(q, k, v, o, torch.cat(sums, dim=2))
+        ctx.group, ctx.scale, ctx.window_size = group, scale, window_size
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        from . import kernels
+
+        q, k, v, o, sums = ctx.saved_tensors
+        group = ctx.group
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        C = q.shape[2] // 2
+        full = _cp_gather_kv(k, v, group)
+        T = full.shape[3]
+        dk_full = torch.zeros(full.shape[1:], dtype=torch.float32, device=q.device)
+        dv_full = torch.zeros_like(dk_full)
+        dqs = []
+        for i, c in enumerate(zigzag_chunk_ids(world, rank)):
+            sl = slice(i * C, (i + 1) * C)
+            e = (c + 1) * C
+            dq, dk, dv = kernels.sp2norm_flash_attention_chunk_bwd(
+                q[:, :, sl], full[0, :, :, :e], full[1, :, :, :e], o[:, :, sl], do[:, :, sl].contiguous(),
+                sums[:, :, sl].contiguous(), c * C, scale=ctx.scale, window_size=ctx.window_size)
+            dqs.append(dq)
+            dk_full[:, :, :e] += dk.float()
+            dv_full[:, :, :e] += dv.float()
+        assert dk_full.shape[2] == T
+        dk_loc = _reduce_scatter_zigzag(dk_full, group).to(k.dtype)
+        dv_loc = _reduce_scatter_zigzag(dv_full, group).to(v.dtype)
+        return torch.cat(dqs, dim=2), dk_loc, dv_loc, None, None, None
+
+
 def context_parallel_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, group=None, scale=None,
                                window_size: int = 0) -> torch.Tensor:
-    """Causal squareplus attention forward with the sequence split over ranks.
+    """Causal squareplus attention with the sequence split over ranks.
 
     q, k, v are this rank's zig-zag local blocks ``[B, H, 2C, D]`` (see
-    ``zigzag_split``; the global length is T = 2·C·world).  K and V are
-    all-gathered once (NCCL over NVLink on GPUs) and put back in sequence
-    order; each of the rank's two query chunks then runs the tcgen05 forward
+    ``zigzag_split``; the global length is T = 2·C·world).  Forward: K and V
+    are all-gathered once (NCCL over NVLink on GPUs) and put back in sequence
+    order; each of the rank's two query chunks runs the tcgen05 forward
     against its visible key prefix (``sp2norm_flash_attention_chunk`` with the
     chunk's global offset).  The squareplus normalizer is a plain sum, so no
     cross-rank max or rescale is needed: the result equals the single-GPU
-    forward.  Returns the rank's output in the same zig-zag local layout.
-    Forward only (like the reference's RoPE / FP8 / paged entry points).
+    forward.  Backward (autograd): K/V are gathered again, each local chunk
+    runs ``sp2norm_flash_attention_chunk_bwd``, dQ stays local and the dK/dV
+    contributions are summed into their owners' chunks by one
+    reduce-scatter.  Returns the rank's output in the zig-zag local layout.
     """
-    from . import kernels
-
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    Tl = q.shape[2]
-    if Tl % 2:
+    if q.shape[2] % 2:
         raise ValueError("the local sequence block must hold two equal zig-zag chunks")
-    C = Tl // 2
-    kv = torch.stack([k, v]).contiguous()
-    full = zigzag_merge(_all_gather(kv, group), dim=3)  # [2, B, Hkv, T, D] in sequence order
-    outs = []
-    for i, c in enumerate(zigzag_chunk_ids(world, rank)):
-        qc = q[:, :, i * C:(i + 1) * C]
-        kp, vp = full[0, :, :, :(c + 1) * C], full[1, :, :, :(c + 1) * C]
-        o, _ = kernels.sp2norm_flash_attention_chunk(qc, kp, vp, c * C, scale=scale, window_size=window_size)
-        outs.append(o)
-    return torch.cat(outs, dim=2)
+    return _ContextParallelAttnFn.apply(q, k, v, group, scale, window_size)

@@ -1,8 +1,8 @@
-"""Context parallelism on the GPU: the query-chunk forward (``sa_flash_fwd_chunk``
-through ``sp2norm_flash_attention_chunk``) against the oracle, chunks that
-reproduce the full forward, and — when two GPUs are visible — two NCCL ranks
-running ``context_parallel_attention`` on zig-zag sequence blocks against the
-single-GPU forward."""
+"""Context parallelism on the GPU: the query-chunk forward and backward
+(``sa_flash_fwd_chunk`` / ``sa_flash_bwd_chunk``) against the oracle, chunks
+that reproduce the full forward and backward, and — when two GPUs are
+visible — two NCCL ranks running ``context_parallel_attention`` forward and
+backward on zig-zag sequence blocks against the single-GPU autograd."""
 
 import os
 import socket
@@ -52,6 +52,54 @@ def test_chunks_reproduce_full_forward(T, chunks, window):
     assert (got.float() - full.float()).abs().max().item() <= 2e-2
 
 
+BWD_TOL = dict(rtol=0.1, atol=5e-2)  # the flash tests' backward tolerance
+
+
+@pytest.mark.parametrize("Tq,Tk,off,D,window,Hq,Hkv", [(128, 256, 128, 128, 0, 4, 2), (100, 300, 200, 64, 0, 2, 2),
+                                                       (256, 1000, 744, 128, 0, 4, 1), (64, 64, 0, 32, 0, 2, 2),
+                                                       (200, 700, 500, 128, 96, 4, 2), (77, 900, 823, 64, 0, 2, 1),
+                                                       (128, 1024, 896, 128, 50, 2, 2)])
+def test_chunk_backward_matches_oracle(Tq, Tk, off, D, window, Hq, Hkv):
+    """dq of the query block and its dk / dv contribution over the key prefix;
+    with a window, keys no query of the block sees get exactly zero."""
+    q = randn((1, Hq, Tq, D), Tq + off, torch.bfloat16, CUDA)
+    k = randn((1, Hkv, Tk, D), Tk, torch.bfloat16, CUDA)
+    v = randn((1, Hkv, Tk, D), Tk + 1, torch.bfloat16, CUDA)
+    do = randn((1, Hq, Tq, D), 7, torch.bfloat16, CUDA)
+    o, rs = sa.sp2norm_flash_attention_chunk(q, k, v, off, window_size=window)
+    dq, dk, dv = sa.kernels.sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, rs, off, window_size=window)
+    rq, rk, rv = O.chunk_flash_attention_bwd(np32(q), np32(k), np32(v), np32(do), off, window_size=window)
+    assert_close(np32(dq), rq, **BWD_TOL)
+    assert_close(np32(dk), rk, **BWD_TOL)
+    assert_close(np32(dv), rv, **BWD_TOL)
+    if window:
+        first_seen = max(0, off - window + 1)
+        assert (dk[:, :, :first_seen] == 0).all() and (dv[:, :, :first_seen] == 0).all()
+
+
+def test_chunked_backward_reproduces_full_backward():
+    T, chunks = 2048, 4
+    q, k, v = (randn((1, h, T, 128), T + h, torch.bfloat16, CUDA) for h in (8, 2, 2))
+    do = randn((1, 8, T, 128), 3, torch.bfloat16, CUDA)
+    qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
+    (sa.sp2norm_flash_attention(qr, kr, vr) * do).sum().backward()
+    C = T // chunks
+    dk_acc = torch.zeros(k.shape, dtype=torch.float32, device=CUDA)
+    dv_acc = torch.zeros_like(dk_acc)
+    dqs = []
+    for c in range(chunks):
+        e = (c + 1) * C
+        qc, doc = q[:, :, c * C:e].contiguous(), do[:, :, c * C:e].contiguous()
+        o, rs = sa.sp2norm_flash_attention_chunk(qc, k[:, :, :e], v[:, :, :e], c * C)
+        dq, dk, dv = sa.kernels.sp2norm_flash_attention_chunk_bwd(qc, k[:, :, :e], v[:, :, :e], o, doc, rs, c * C)
+        dqs.append(dq)
+        dk_acc[:, :, :e] += dk.float()
+        dv_acc[:, :, :e] += dv.float()
+    assert_close(np32(torch.cat(dqs, dim=2)), np32(qr.grad), rtol=2e-2, atol=2e-2)
+    assert_close(np32(dk_acc), np32(kr.grad), rtol=5e-2, atol=5e-2)
+    assert_close(np32(dv_acc), np32(vr.grad), rtol=5e-2, atol=5e-2)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -72,10 +120,23 @@ def _cp_worker(rank, world, port, q):
     try:
         g = torch.Generator().manual_seed(5)
         qf, kf, vf = (torch.randn(1, h, 4096, 128, generator=g).to(torch.bfloat16).cuda() for h in (16, 4, 4))
-        o_local = context_parallel_attention(*(zigzag_split(t, world, rank) for t in (qf, kf, vf)))
-        o = zigzag_merge(_all_gather(o_local))
-        ref = sa.sp2norm_flash_attention(qf, kf, vf)
-        q.put((rank, "ok", float((o.float() - ref.float()).abs().max())))
+        dof = torch.randn(1, 16, 4096, 128, generator=g).to(torch.bfloat16).cuda()
+        loc = [zigzag_split(t, world, rank).requires_grad_(True) for t in (qf, kf, vf)]
+        o_local = context_parallel_attention(*loc)
+        (o_local * zigzag_split(dof, world, rank)).sum().backward()
+        o = zigzag_merge(_all_gather(o_local.detach()))
+        grads = [zigzag_merge(_all_gather(t.grad)) for t in loc]
+        full = [t.clone().requires_grad_(True) for t in (qf, kf, vf)]
+        ref = sa.sp2norm_flash_attention(*full)
+        (ref * dof).sum().backward()
+        # allclose-style count of elements off by more than atol + rtol * |ref|
+        # (bf16 gradients: the chunked dK/dV are sums of per-chunk bf16 partials)
+        def bad(a, b, tol):
+            a, b = a.detach().float(), b.detach().float()
+            return int(((a - b).abs() > tol + tol * b.abs()).sum())
+
+        nbad = bad(o, ref, 2e-2) + sum(bad(a, b.grad, 5e-2) for a, b in zip(grads, full))
+        q.put((rank, "ok", nbad))
     except Exception as e:  # report, never hang
         q.put((rank, "error", repr(e)[:200]))
     finally:
@@ -103,4 +164,4 @@ def test_context_parallel_two_gpus_equals_single_gpu():
             pytest.fail("rank did not finish")
     res = sorted(q.get(timeout=5) for _ in range(2))
     assert [r[1] for r in res] == ["ok", "ok"], res
-    assert all(r[2] <= 2e-2 for r in res), res
+    assert all(r[2] == 0 for r in res), res

@@ -73,6 +73,28 @@ def test_oracle_query_chunks_reproduce_full_attention(window):
     np.testing.assert_allclose(np.concatenate(parts, axis=2), full, rtol=1e-5, atol=1e-6)
 
 
+def test_oracle_query_chunks_reproduce_full_backward():
+    g = np.random.default_rng(4)
+    q = g.standard_normal((1, 4, 48, 16)).astype(np.float32)
+    k = g.standard_normal((1, 2, 48, 16)).astype(np.float32)
+    v = g.standard_normal((1, 2, 48, 16)).astype(np.float32)
+    do = g.standard_normal((1, 4, 48, 16)).astype(np.float32)
+    rq, rk, rv = O.sp2norm_flash_attention_bwd(q, k, v, do, window_size=9)
+    C = 12
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    dqs = []
+    for c in range(4):
+        e = (c + 1) * C
+        gq, gk, gv = O.chunk_flash_attention_bwd(q[:, :, c * C:e], k[:, :, :e], v[:, :, :e], do[:, :, c * C:e],
+                                                 c * C, window_size=9)
+        dqs.append(gq)
+        dk[:, :, :e] += gk
+        dv[:, :, :e] += gv
+    for a, b in ((np.concatenate(dqs, axis=2), rq), (dk, rk), (dv, rv)):
+        np.testing.assert_allclose(a, b, rtol=1e-4, atol=1e-5)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -88,24 +110,37 @@ def _worker(rank, world, port, mode, q):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
     try:
         if mode.startswith("cp"):
-            # context parallelism: the gather / reorder / chunk logic, with the
-            # chunk kernel replaced by the oracle (CPU ranks, no GPU)
+            # context parallelism: the gather / reorder / chunk / reduce-scatter
+            # logic, forward and backward, with the chunk kernels replaced by
+            # the oracle (CPU ranks, no GPU)
             import smooth_attn.kernels as K
 
             def chunk(qc, kp, vp, off, scale=None, window_size=0):
                 o = O.chunk_flash_attention(qc.numpy(), kp.numpy(), vp.numpy(), off, scale=scale,
                                             window_size=window_size)
-                return torch.from_numpy(o), None
+                return torch.from_numpy(o), torch.ones(qc.shape[:3])
+
+            def chunk_bwd(qc, kp, vp, o, do, sums, off, scale=None, window_size=0):
+                g = O.chunk_flash_attention_bwd(qc.detach().numpy(), kp.detach().numpy(), vp.detach().numpy(),
+                                                do.numpy(), off, scale=scale, window_size=window_size)
+                return tuple(torch.from_numpy(t) for t in g)
 
             K.sp2norm_flash_attention_chunk = chunk
+            K.sp2norm_flash_attention_chunk_bwd = chunk_bwd
             window = int(mode[2:] or 0)
             g = torch.Generator().manual_seed(1)
             qf, kf, vf = (torch.randn(2, h, 40, 8, generator=g) for h in (4, 2, 2))
-            o_local = context_parallel_attention(*(zigzag_split(t, world, rank) for t in (qf, kf, vf)),
-                                                 window_size=window)
-            o = zigzag_merge(_all_gather(o_local))
+            dof = torch.randn(2, 4, 40, 8, generator=g)
+            loc = [zigzag_split(t, world, rank).requires_grad_(True) for t in (qf, kf, vf)]
+            o_local = context_parallel_attention(*loc, window_size=window)
+            (o_local * zigzag_split(dof, world, rank)).sum().backward()
+            o = zigzag_merge(_all_gather(o_local.detach()))
+            grads = [zigzag_merge(_all_gather(t.grad)) for t in loc]
             ref = O.sp2norm_flash_attention(qf.numpy(), kf.numpy(), vf.numpy(), window_size=window)
-            q.put((rank, "ok", float(np.abs(o.numpy() - ref).max())))
+            rg = O.sp2norm_flash_attention_bwd(qf.numpy(), kf.numpy(), vf.numpy(), dof.numpy(), window_size=window)
+            err = max([float(np.abs(o.numpy() - ref).max())] +
+                      [float(np.abs(a.numpy() - b).max()) for a, b in zip(grads, rg)])
+            q.put((rank, "ok", err))
             return
         g = torch.Generator().manual_seed(0)
         x = torch.randn(3, 5, 12, 12, generator=g)  # 15 units: uneven split
