@@ -177,6 +177,13 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"metric": "fused squareplus-attn fwd+bwd TFLOP/s", "n_gpus": world, **flash}), flush=True)
         return
+    if args.only == "cp":
+        g = torch.Generator(device="cuda").manual_seed(99 + rank)
+        shape = tuple(int(v) for v in args.shape.split(",")) if args.shape else CP_SHAPE
+        res = extra_cp(shape, args.steps, world, rank, g, tf_sus)
+        if rank == 0:
+            print(json.dumps({"workload": "cp", "n_gpus": world, "steps": args.steps, **res}), flush=True)
+        return
     if args.only in ("decode", "rope", "fp8"):  # one extension workload (profiling entry point)
         g = torch.Generator(device="cuda").manual_seed(777 + rank)
         shape = tuple(int(v) for v in args.shape.split(",")) if args.shape else None
@@ -266,10 +273,6 @@ def run_ours(args):
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
 
 
 def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
@@ -412,6 +415,39 @@ DECODE_SHAPES = ((1, 32, 8, 8192, 128, 16), (1, 32, 8, 32768, 128, 16), (8, 32, 
                  (64, 32, 8, 4096, 128, 16))
 ROPE_SHAPES = ((2, 32, 1024, 128), (4, 12, 512, 64), (2, 32, 8192, 128))  # tests/test_rope_proj.py:162-163 + long
 FP8_SHAPES = ((4, 8, 1024, 64), (2, 32, 8192, 128))  # tests/test_fp8_flash.py:126-127 + long
+CP_SHAPE = (1, 32, 65536, 128)  # one long sequence split over the ranks (context parallelism)
+
+
+def extra_cp(shape, steps, world, rank, g, tf_sus):
+    """Context-parallel causal attention fwd+bwd over the ranks (strong scaling:
+    one sequence, total work fixed): TFLOP/s of the whole job, K/V all-gather
+    and dK/dV reduce-scatter inside the timed region."""
+    import smooth_attn.parallel as par
+    from oracle import sa_oracle as O
+
+    B, H, T, D = shape
+    dev = torch.device("cuda")
+    w = max(world, 1)
+    if T % (2 * w):
+        raise SystemExit(f"T={T} must divide into 2*world chunks")
+    loc = [torch.randn(B, H, T // w, D, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+           for _ in range(3)]
+    do = torch.randn(B, H, T // w, D, device=dev, generator=g).to(torch.bfloat16)
+    if world > 1:
+        step = lambda: torch.autograd.backward(par.context_parallel_attention(*loc), do)  # noqa: E731
+    else:  # one rank: the plain single-GPU autograd forward + backward
+        import smooth_attn as sa
+
+        step = lambda: torch.autograd.backward(sa.sp2norm_flash_attention(*loc), do)  # noqa: E731
+    for _ in range(2):
+        step()
+    ms = time_steps(step, steps, world) / steps
+    fl = O.flash_flops(B, H, T, D) + O.flash_flops(B, H, T, D, bwd=True)
+    return {"config": f"context-parallel fwd+bwd, bf16 [{B},{H},{T},{D}] split over {w} rank(s), "
+                      "zig-zag chunks, NCCL all-gather K/V + reduce-scatter dK/dV", "scaling": "strong",
+            "ms": round(ms, 3), "TFLOP/s_all": round(fl / (ms * 1e-3) / 1e12, 1),
+            "TFLOP/s_per_gpu": round(fl / (ms * 1e-3) / 1e12 / w, 1),
+            "frac_of_sustained_per_gpu": round(fl / (ms * 1e-3) / 1e12 / w / tf_sus, 3)}
 
 
 def _gbs(nbytes, ms):
@@ -573,10 +609,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--skip-flash", action="store_true")
-    ap.add_argument("--only", choices=("all", "norm", "flash", "decode", "rope", "fp8"), default="all",
+    ap.add_argument("--only", choices=("all", "norm", "flash", "decode", "rope", "fp8", "cp"), default="all",
                     help="run one workload only (small-case profiling)")
     ap.add_argument("--shape", default=None,
-                    help="with --only decode: B,Hq,Hkv,T,D,block_size; rope / fp8: B,H,T,D (one shape)")
+                    help="with --only decode: B,Hq,Hkv,T,D,block_size; rope / fp8 / cp: B,H,T,D (one shape)")
     ap.add_argument("--norm-batch", type=int, default=NORM_CFG["B"],
                     help="B of the causal-norm workload [B,16,2048,2048] (BASELINE: 8)")
     ap.add_argument("--flash-shape", default=",".join(str(FLASH_CFG[k]) for k in "BHTD"),
@@ -590,7 +626,13 @@ def main():
     if args.impl == "reference":
         run_reference(args)
     else:
-        run_ours(args)
+        try:
+            run_ours(args)
+        finally:  # every path, the single-workload ones included, leaves the process group cleanly
+            import torch.distributed as dist
+
+            if dist.is_available() and dist.is_initialized():
+                dist.destroy_process_group()
 
 
 if __name__ == "__main__":
