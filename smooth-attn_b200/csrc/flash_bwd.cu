@@ -221,8 +221,12 @@ __global__ void __launch_bounds__(192, 1)
   BwdBars* bars = reinterpret_cast<BwdBars*>(smem + C::OFF_BAR);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * C::BN;
-  const int b = blockIdx.y / p.Hkv, kvh = blockIdx.y % p.Hkv;
+  int kvt, bhk;  // KV tile (0 = most query tiles) and (batch, kv head)
+  // one head at a time (group of 1): measured faster here than the grouped
+  // order the forward uses, which lengthened this kernel's step
+  grouped_longest_first((int)blockIdx.x, (p.Tk + C::BN - 1) / C::BN, p.B * p.Hkv, 1, kvt, bhk);
+  const int n0 = kvt * C::BN;
+  const int b = bhk / p.Hkv, kvh = bhk % p.Hkv;
   const int G = p.Hq / p.Hkv;
   int qt_first, qt_last;
   query_tile_range(p, n0, C::BN, C::BQ, qt_first, qt_last);
@@ -582,8 +586,12 @@ __global__ void __launch_bounds__(448, 1)
   Bwd128Bars* bars = reinterpret_cast<Bwd128Bars*>(smem + C::OFF_BAR);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * C::BN;
-  const int b = blockIdx.y / p.Hkv, kvh = blockIdx.y % p.Hkv;
+  int kvt, bhk;  // KV tile (0 = most query tiles) and (batch, kv head)
+  // one head at a time (group of 1): measured faster here than the grouped
+  // order the forward uses, which lengthened this kernel's step
+  grouped_longest_first((int)blockIdx.x, (p.Tk + C::BN - 1) / C::BN, p.B * p.Hkv, 1, kvt, bhk);
+  const int n0 = kvt * C::BN;
+  const int b = bhk / p.Hkv, kvh = bhk % p.Hkv;
   const int G = p.Hq / p.Hkv;
   int qt_first, qt_last;
   query_tile_range(p, n0, C::BN, C::BQ, qt_first, qt_last);
@@ -953,6 +961,7 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
                       int64_t qoff = 0) {
   using C = BwdCfg<D>;
   if (Tk < 0) Tk = T;
+  if (((Tk + C::BN - 1) / C::BN) * B * Hkv > INT32_MAX) return SA_ERR_UNSUPPORTED;  // 1-D grid, before any launch
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int64_t rows = B * Hq * T;
   int prep_dev = 0, prep_sms = 148;
@@ -986,7 +995,7 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
   p.qoff = (int)qoff;
   p.window = (int)window;
   p.scale = scale;
-  dim3 grid((unsigned)((Tk + C::BN - 1) / C::BN), (unsigned)(B * Hkv));
+  dim3 grid((unsigned)(((Tk + C::BN - 1) / C::BN) * B * Hkv));
   if constexpr (D == 128) {
     CUtensorMap mq64, mdo64;
     if (!make_map_4d(&mq64, q, BF16, B, Hq, T, D, qs, 64, Bwd128::BQ) ||

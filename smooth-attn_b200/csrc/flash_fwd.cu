@@ -193,8 +193,9 @@ __global__ void __launch_bounds__(320, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + C::OFF_BAR);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pair = p.npairs - 1 - (int)blockIdx.x;  // longest (most KV tiles) first
-  const int bh = blockIdx.y;
+  int xr, bh;
+  grouped_longest_first((int)blockIdx.x, p.npairs, p.B * p.Hq, kHeadGroup, xr, bh);
+  const int pair = p.npairs - 1 - xr;  // x = 0: the pair with the most KV tiles
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvh = h / (p.Hq / p.Hkv);
   const int qbase = pair * 2 * C::BM;
@@ -481,7 +482,8 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, floa
   p.dscale = dscale;
   auto kern = flash_fwd_kernel<D, BF16, EXACT, QK8>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  dim3 grid(p.npairs, (unsigned)(B * Hq));
+  if ((int64_t)p.npairs * B * Hq > INT32_MAX) return SA_ERR_UNSUPPORTED;  // 1-D grid of (pair, head) CTAs
+  dim3 grid((unsigned)(p.npairs * B * Hq));
   kern<<<grid, C::THREADS, C::SMEM, st>>>(mq, mk, mv, p);
   return SA_OK;
 }

@@ -20,6 +20,24 @@
 namespace sa {
 namespace sm100 {
 
+// ---- CTA order for causal attention --------------------------------------------
+
+// Linear CTA index -> (x, y) for an nx-by-ny grid whose x = 0 CTAs carry the
+// most work (causal: the longest KV range).  Heads (y) go in groups of gsz;
+// inside a group all heads' x = 0 CTAs launch first, then x = 1, ...  Long
+// CTAs therefore start early and the grid ends on short ones, while only
+// about two groups of heads are in flight at once (their K/V stay in L2).
+__device__ __forceinline__ void grouped_longest_first(int idx, int nx, int ny, int gsz, int& x, int& y) {
+  const int g = idx / (gsz * nx);
+  const int y0 = g * gsz;
+  const int ge = min(gsz, ny - y0);
+  const int r = idx - g * gsz * nx;
+  x = r / ge;
+  y = y0 + (r - x * ge);
+}
+
+constexpr int kHeadGroup = 8;
+
 // ---- TMA -------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
