@@ -187,6 +187,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   // zero both P buffers once: head rows past the group stay zero
   for (int i = threadIdx.x; i < 2 * 8192 / 16; i += THREADS)
     reinterpret_cast<uint4*>(smem + OFF_P)[i] = make_uint4(0u, 0u, 0u, 0u);
+  // The producers start their first unit's context-length and block-table
+  // loads now, so those DRAM round trips overlap the setup barrier.
+  int pre_wu = -1, pre_wp = 0, pre_win = 0;
+  if (warp == 0 || warp == 6) {
+    const Unit U0 = item_of(a, u_first, x0, x1);
+    pre_wu = u_first;
+    pre_wp = U0.t_lo * (TOK / a.bs);
+    if (pre_wp + lane < a.max_blocks) pre_win = __ldg(a.bt + (int64_t)U0.b * a.max_blocks + pre_wp + lane);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -217,7 +226,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* ring = smem + (isv ? OFF_V : OFF_K);
     if (lane == 0) tma_prefetch_desc(map);
     int n = 0;
-    int wu = -1, wp = 0, win = 0;  // block-table window: lane l holds page wp + l of unit wu
+    int wu = pre_wu, wp = pre_wp, win = pre_win;  // block-table window: lane l holds page wp + l of unit wu
     for (int k = 0; !failed; ++k) {
       int id;
       if (!isv) {  // warp 0 publishes the k-th item
@@ -466,46 +475,40 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       __threadfence();
       const int nsl = U.nslots;
-      // Head sums: one warp, lanes stride the slots, shuffle sum (fixed order).
-      if (e < 32) {
-        float t[NH];
-#pragma unroll
-        for (int g = 0; g < NH; ++g) t[g] = 0.f;
-        for (int sl = e; sl < nsl; sl += 32)
-#pragma unroll
-          for (int g = 0; g < NH; ++g)
-            if (g < a.GT) t[g] += __ldcg(base + (int64_t)sl * REC + a.GT * D + g);
-#pragma unroll
-        for (int g = 0; g < NH; ++g) {
-#pragma unroll
-          for (int m = 16; m > 0; m >>= 1) t[g] += __shfl_xor_sync(0xffffffffu, t[g], m);
-          if (e == 0) red[4 * NH + g] = t[g] + eps4;
-        }
-      }
-      ew_sync();  // head sums in red[4 * NH ..]
-      // O: thread e owns float4 groups f = e, e + 128, ... of the GT x D block;
-      // slots are added in index order, 8 independent 16-byte loads in flight.
+      // Thread e owns float4 groups f = e, e + 128, ... of the GT x D block and
+      // adds, slot by slot in index order (deterministic), both its O values
+      // and its head's sum: one pass, up to 16 slots of independent loads in
+      // flight, no barrier.
       const int nf = a.GT * D / 4;
       for (int f = e; f < nf; f += 128) {
+        const int g = (4 * f) / D;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float sy = 0.f;
         int sl = 0;
-        for (; sl + 8 <= nsl; sl += 8) {
-          float4 v[8];
+        for (; sl + 16 <= nsl; sl += 16) {
+          float4 v[16];
+          float w[16];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
+          for (int j = 0; j < 16; ++j) {
             v[j] = __ldcg(reinterpret_cast<const float4*>(base + (int64_t)(sl + j) * REC) + f);
+            w[j] = __ldcg(base + (int64_t)(sl + j) * REC + a.GT * D + g);
+          }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc.x += v[j].x, acc.y += v[j].y, acc.z += v[j].z, acc.w += v[j].w;
+          for (int j = 0; j < 16; ++j) {
+            acc.x += v[j].x, acc.y += v[j].y, acc.z += v[j].z, acc.w += v[j].w;
+            sy += w[j];
+          }
         }
         for (; sl < nsl; ++sl) {
           const float4 v = __ldcg(reinterpret_cast<const float4*>(base + (int64_t)sl * REC) + f);
+          sy += __ldcg(base + (int64_t)sl * REC + a.GT * D + g);
           acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
         }
-        const float inv = 1.0f / red[4 * NH + (4 * f) / D];
-        uint2 w;
-        w.x = pack2_bf16(acc.x * inv, acc.y * inv);
-        w.y = pack2_bf16(acc.z * inv, acc.w * inv);
-        *reinterpret_cast<uint2*>(a.out + ((int64_t)U.b * a.Hq + U.hq0) * D + 4 * f) = w;
+        const float inv = 1.0f / (sy + eps4);
+        uint2 wo;
+        wo.x = pack2_bf16(acc.x * inv, acc.y * inv);
+        wo.y = pack2_bf16(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(a.out + ((int64_t)U.b * a.Hq + U.hq0) * D + 4 * f) = wo;
       }
       if (e == 0) a.tickets[U.u] = 0;  // ready for the next call
       id = id_next;
