@@ -56,11 +56,22 @@ __global__ void __launch_bounds__(256) fp8_absmax_kernel(Fp8Src s, unsigned* __r
   for (int t = 0; t < 3; ++t) {
     const T* x = static_cast<const T*>(s.p[t]);
     float m = 0.f;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < s.n[t] / 8; i += stride) {
+    const int64_t nv = s.n[t] / 8;
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < nv; i += 4 * stride) {  // four independent 16-byte loads in flight
+      float f[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) load8<T>(x + (i + j * stride) * 8, f[j]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[j][e]));  // NaN inputs are dropped by fmaxf
+    }
+    for (; i < nv; i += stride) {
       float f[8];
       load8<T>(x + i * 8, f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[e]));  // NaN inputs are dropped by fmaxf
+      for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[e]));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
