@@ -425,11 +425,30 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_bwd_bulk(const T* __rest
       unpack<T, VEC>(sx + (size_t)v * 16, xf);
       unpack<TG, VEC>(sg + (size_t)v * GB, gf);
       const int lim = (CAUSAL && v == nvis - 1) ? qe : VEC - 1;
+      if constexpr (P2 && VEC % 2 == 0) {
+        // power 2: pairs of elements per packed fp32x2 instruction
+        // (bit-identical per element; the sums keep two partial lanes)
+        float2 sy2 = make_float2(0.f, 0.f), sgy2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const float yy = e <= lim ? y_scaled<P2>(xf[e], c1, c0, power) : 0.f;
-        sum_y += yy;
-        sum_gy = fmaf(gf[e], yy, sum_gy);
+        for (int e = 0; e < VEC; e += 2) {
+          const float2 a = ffma2(make_float2(xf[e], xf[e + 1]), make_float2(c1, c1), make_float2(c0, c0));
+          const float2 u = ffma2(a, a, make_float2(4.0f, 4.0f));
+          const float2 t = ffma2(u, make_float2(rsqrt_approx(u.x), rsqrt_approx(u.y)), a);
+          float2 yy = fmul2(t, t);
+          yy.x = e <= lim ? yy.x : 0.f;
+          yy.y = e + 1 <= lim ? yy.y : 0.f;
+          sy2 = fadd2(sy2, yy);
+          sgy2 = ffma2(make_float2(gf[e], gf[e + 1]), yy, sgy2);
+        }
+        sum_y += sy2.x + sy2.y;
+        sum_gy += sgy2.x + sgy2.y;
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float yy = e <= lim ? y_scaled<P2>(xf[e], c1, c0, power) : 0.f;
+          sum_y += yy;
+          sum_gy = fmaf(gf[e], yy, sum_gy);
+        }
       }
     }
     const float Sp = rowsum != nullptr ? __ldg(rowsum + row) * s_scale : warp_sum(sum_y) + eps_s;  // S' = 2^p S
@@ -444,21 +463,35 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_bwd_bulk(const T* __rest
         unpack<T, VEC>(sx + (size_t)v * 16, xf);
         unpack<TG, VEC>(sg + (size_t)v * GB, gf);
         const int lim = (CAUSAL && v == nvis - 1) ? qe : VEC - 1;
+        if constexpr (P2 && VEC % 2 == 0) {
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const float a = fmaf(xf[e], c1, c0);
-          const float u = fmaf(a, a, 4.0f);
-          const float r = rsqrt_approx(u);
-          const float w = fmaf(a, r, 1.0f);
-          float dydx = kr * w;
-          if (P2) {
-            dydx *= fmaf(u, r, a);
-          } else if (power >= 2) {
-            const float t = fmaf(u, r, a);
-            dydx *= t;
-            if (power == 3) dydx *= t;
+          for (int e = 0; e < VEC; e += 2) {
+            const float2 a = ffma2(make_float2(xf[e], xf[e + 1]), make_float2(c1, c1), make_float2(c0, c0));
+            const float2 u = ffma2(a, a, make_float2(4.0f, 4.0f));
+            const float2 r = make_float2(rsqrt_approx(u.x), rsqrt_approx(u.y));
+            const float2 w = ffma2(a, r, make_float2(1.0f, 1.0f));
+            const float2 dydx = fmul2(fmul2(make_float2(kr, kr), w), ffma2(u, r, a));
+            const float2 res = fmul2(dydx, fsub2(make_float2(gf[e], gf[e + 1]), make_float2(dot, dot)));
+            o.set(e, e <= lim ? res.x : 0.f);
+            o.set(e + 1, e + 1 <= lim ? res.y : 0.f);
           }
-          o.set(e, e <= lim ? dydx * (gf[e] - dot) : 0.f);
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const float a = fmaf(xf[e], c1, c0);
+            const float u = fmaf(a, a, 4.0f);
+            const float r = rsqrt_approx(u);
+            const float w = fmaf(a, r, 1.0f);
+            float dydx = kr * w;
+            if (P2) {
+              dydx *= fmaf(u, r, a);
+            } else if (power >= 2) {
+              const float t = fmaf(u, r, a);
+              dydx *= t;
+              if (power == 3) dydx *= t;
+            }
+            o.set(e, e <= lim ? dydx * (gf[e] - dot) : 0.f);
+          }
         }
       } else {
         o.zero();
