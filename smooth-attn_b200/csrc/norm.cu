@@ -301,8 +301,20 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __rest
           if (v < nvis) {
             float xf[VEC];
             unpack<T, VEC>(slot + (size_t)v * 16, xf);
+            if constexpr (P2 && VEC % 2 == 0) {  // pairs per packed fp32x2 instruction
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) y[c][e] = y_scaled<P2>(xf[e], c1, c0, power);
+              for (int e = 0; e < VEC; e += 2) {
+                const float2 a = ffma2(make_float2(xf[e], xf[e + 1]), make_float2(c1, c1), make_float2(c0, c0));
+                const float2 u = ffma2(a, a, make_float2(4.0f, 4.0f));
+                const float2 t = ffma2(u, make_float2(rsqrt_approx(u.x), rsqrt_approx(u.y)), a);
+                const float2 yy = fmul2(t, t);
+                y[c][e] = yy.x;
+                y[c][e + 1] = yy.y;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) y[c][e] = y_scaled<P2>(xf[e], c1, c0, power);
+            }
             if (CAUSAL && v == nvis - 1) {
 #pragma unroll
               for (int e = 0; e < VEC; ++e) y[c][e] = e > qe ? 0.f : y[c][e];
@@ -324,7 +336,11 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __rest
           Pack<T, VEC> o;
           if (32 * c < nvis && v < nvis) {
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) o.set(e, y[c][e] * inv);
+            for (int e = 0; e < VEC; e += 2) {
+              const float2 r = fmul2(make_float2(y[c][e], y[c][e + 1]), make_float2(inv, inv));
+              o.set(e, r.x);
+              o.set(e + 1, r.y);
+            }
           } else {
             o.zero();
           }
