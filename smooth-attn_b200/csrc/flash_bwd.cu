@@ -472,7 +472,11 @@ struct Bwd128Bars {
   uint64_t s_full[2];   // S^T of tile j ready in buffer j&1
   uint64_t dp_full[2];  // dP^T of tile j ready in buffer j&1
   uint64_t p_ready;    // elementwise stage of tile j done (256 arrivals)
-  uint64_t mm2_done;   // dK(j), dQ^T(j) complete
+  // dK(j), dQ^T(j) complete, in barrier j&1.  The drain releases dq_free
+  // before its atomics, so the MMA can finish tile j+2 before the drain waits
+  // for tile j+1; one barrier per tile parity keeps each barrier at most one
+  // phase ahead of its waiter (a single barrier could complete twice).
+  uint64_t mm2_done[2];
   uint64_t dq_free;    // dQ^T(j) read out of TMEM (128 arrivals): dP^T buffer j&1 free
   uint64_t all_done;
   uint32_t tmem_base;
@@ -622,7 +626,7 @@ __global__ void __launch_bounds__(448, 1)
     for (int i = 0; i < 2; ++i) mbar_init(&bars->s_full[i], 1);
     for (int i = 0; i < 2; ++i) mbar_init(&bars->dp_full[i], 1);
     mbar_init(&bars->p_ready, 256);
-    mbar_init(&bars->mm2_done, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->mm2_done[i], 1);
     mbar_init(&bars->dq_free, 128);
     mbar_init(&bars->all_done, 1);
     fence_mbar_init();
@@ -733,7 +737,7 @@ __global__ void __launch_bounds__(448, 1)
           for (int kk = 0; kk < C::BN / 16; ++kk) {  // dQ^T = K^T dS^T into dP^T buffer bb (consumed)
             mma_ss(tbase + 128 + bb * 64, desc_add(dKt0, kk * 16 * 128), desc_add(bds0, kk * 16 * 128), id_dq, kk > 0);
           }
-          mma_commit(&bars->mm2_done);
+          mma_commit(&bars->mm2_done[bb]);
           mma_commit(&bars->q_empty[st]);
           if (it + 2 < ntiles) {
             const int nx = it + 2;
@@ -758,7 +762,7 @@ __global__ void __launch_bounds__(448, 1)
     Cursor cur{kvh * G, qt_first};
     for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
       // polling (not suspending): the drain's reaction time gates the next dP^T
-      if (!b_warp_wait_spin(&bars->mm2_done, it & 1, failed)) break;
+      if (!b_warp_wait_spin(&bars->mm2_done[it & 1], (it >> 1) & 1, failed)) break;
       tc_fence_after();
       uint32_t v0[32], v1[32];
       tmem_ld32(tl + 128 + (it & 1) * 64, v0);  // dQ^T(it) sits in dP^T buffer it&1
