@@ -162,6 +162,30 @@ def _is_winner_family(family):
     return family.cache_key == DEFAULT_FAMILY.cache_key
 
 
+def _tracing(*tensors):
+    """True under torch.compile / make_fx / export: the kernels must then be
+    reached through the torch.library ops in ``_ops.py`` (a ctypes launch
+    is not traceable, and fake tensors have no data pointer)."""
+    if torch.compiler.is_compiling():
+        return True
+    from torch._subclasses.fake_tensor import FakeTensor
+    from torch._subclasses.functional_tensor import FunctionalTensor
+    from torch.fx.experimental.proxy_tensor import get_proxy_mode
+
+    if get_proxy_mode() is not None:
+        return True
+    return any(isinstance(t, (FakeTensor, FunctionalTensor)) for t in tensors)
+
+
+def _ops():
+    return torch.ops.smooth_attn_b200
+
+
+def _norm_meta(family, causal, rows, cols):
+    variant = ("squareplus_winner" if _is_winner_family(family) else "squareplus_family") + "_b200"
+    return {"variant": variant, "causal": bool(causal), "rows": rows, "cols": cols, "kernel": "sa_norm_fwd"}
+
+
 # ---------------------------------------------------------------------------
 # normalization forward / backward launchers
 # ---------------------------------------------------------------------------
@@ -169,6 +193,19 @@ def _is_winner_family(family):
 
 def _launch_norm_fwd(x2d, out2d, family, causal, rowsum=None):
     """x2d/out2d: contiguous [rows, cols] CUDA tensors of the same dtype."""
+    if _tracing(x2d, out2d):
+        rows, cols = x2d.shape
+        _check_cols(cols)
+        res, rs = _ops().norm_fwd(x2d, float(family.alpha), float(family.theta), int(family.power), bool(causal),
+                                  rowsum is not None)
+        out2d.copy_(res)
+        if rowsum is not None:
+            rowsum.copy_(rs)
+        return _norm_meta(family, causal, rows, cols)
+    return _norm_fwd_direct(x2d, out2d, family, causal, rowsum)
+
+
+def _norm_fwd_direct(x2d, out2d, family, causal, rowsum=None):
     rows, cols = x2d.shape
     _check_cols(cols)
     with torch.cuda.device(x2d.device):
@@ -179,11 +216,20 @@ def _launch_norm_fwd(x2d, out2d, family, causal, rowsum=None):
             _stream(x2d),
         )
     _lib.check(st, "sa_norm_fwd")
-    variant = ("squareplus_winner" if _is_winner_family(family) else "squareplus_family") + "_b200"
-    return {"variant": variant, "causal": bool(causal), "rows": rows, "cols": cols, "kernel": "sa_norm_fwd"}
+    return _norm_meta(family, causal, rows, cols)
 
 
 def _launch_norm_bwd(x2d, g2d, rowsum, dx2d, family, causal):
+    if _tracing(x2d, g2d, rowsum, dx2d):
+        assert causal
+        _check_cols(x2d.shape[1])
+        dx2d.copy_(_ops().norm_causal_bwd(x2d, g2d, rowsum, float(family.alpha), float(family.theta),
+                                          int(family.power)))
+        return
+    _norm_bwd_direct(x2d, g2d, rowsum, dx2d, family, causal)
+
+
+def _norm_bwd_direct(x2d, g2d, rowsum, dx2d, family, causal):
     rows, cols = x2d.shape
     _check_cols(cols)
     with torch.cuda.device(x2d.device):
@@ -206,8 +252,12 @@ def softplus_norm_triton(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.the
     family = _resolve_family(alpha, theta, power, family)
     x_row = _prepare_rowwise_input(x)
     _check_cols(x_row.shape[1])
-    out = torch.empty_like(x_row)
-    meta = _launch_norm_fwd(x_row, out, family, causal=False)
+    if _tracing(x_row):
+        out, _ = _ops().norm_fwd(x_row, float(family.alpha), float(family.theta), int(family.power), False, False)
+        meta = _norm_meta(family, False, *x_row.shape)
+    else:
+        out = torch.empty_like(x_row)
+        meta = _launch_norm_fwd(x_row, out, family, causal=False)
     return (out, meta) if return_meta else out
 
 
@@ -243,6 +293,12 @@ def softplus_norm_causal_triton(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAM
                                 power=DEFAULT_FAMILY.power, *, family=None, return_meta=False):
     family = _resolve_family(alpha, theta, power, family)
     x_attn = _prepare_attention_input(x)
+    if _tracing(x_attn):
+        L = x_attn.shape[-1]
+        _check_cols(L)
+        out, _ = _ops().norm_fwd(x_attn, float(family.alpha), float(family.theta), int(family.power), True, False)
+        meta = _norm_meta(family, True, x_attn.numel() // max(L, 1), L)
+        return (out, meta) if return_meta else out
     out = torch.empty_like(x_attn)
     return softplus_norm_causal_triton_out(out, x_attn, family=family, return_meta=return_meta)
 
@@ -264,9 +320,13 @@ class _SoftplusNormCausalAutogradFn(torch.autograd.Function):
         family = FamilyConfig(alpha=float(alpha), theta=float(theta), power=int(power))
         x_attn = _prepare_attention_input(x)
         L = x_attn.shape[-1]
-        out = torch.empty_like(x_attn)
-        rowsum = torch.empty(x_attn.numel() // max(L, 1), device=x_attn.device, dtype=torch.float32)
-        result, _ = _causal_out(out, x_attn, family, rowsum=rowsum)
+        if _tracing(x_attn):
+            _check_cols(L)
+            result, rowsum = _ops().norm_fwd(x_attn, family.alpha, family.theta, family.power, True, True)
+        else:
+            out = torch.empty_like(x_attn)
+            rowsum = torch.empty(x_attn.numel() // max(L, 1), device=x_attn.device, dtype=torch.float32)
+            result, _ = _causal_out(out, x_attn, family, rowsum=rowsum)
         ctx.family = family
         ctx.save_for_backward(x_attn, rowsum)
         return result
@@ -278,6 +338,9 @@ class _SoftplusNormCausalAutogradFn(torch.autograd.Function):
         x, rowsum = ctx.saved_tensors
         L = x.shape[-1]
         g = grad_output.contiguous()
+        if _tracing(x, g, rowsum):
+            f = ctx.family
+            return _ops().norm_causal_bwd(x, g, rowsum, f.alpha, f.theta, f.power), None, None, None
         dx = torch.empty_like(x)
         _launch_norm_bwd(x.view(-1, L), g.view(-1, L), rowsum, dx.view(-1, L), ctx.family, causal=True)
         return dx, None, None, None
@@ -427,11 +490,18 @@ def _flash_check(q, k, v):
 
 def _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True):
     """Run the fused forward; return (o, row_sums) like kernels.py:1912-1931."""
+    if _tracing(q, k, v):
+        return _ops().flash_fwd(q, k, v, float(scale), int(window_size), bool(use_fast_sqrt))
+    return _flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt)
+
+
+def _flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt, o=None):
     B, H_q, T, D = q.shape
     H_kv = k.shape[1]
-    o = torch.empty_like(q)
-    if not (o.stride(3) == 1 and all((s * o.element_size()) % 16 == 0 for s in o.stride()[:3])):
-        o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    if o is None:
+        o = torch.empty_like(q)
+        if not (o.stride(3) == 1 and all((s * o.element_size()) % 16 == 0 for s in o.stride()[:3])):
+            o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     row_sums = torch.empty(B, H_q, T, device=q.device, dtype=torch.float32)
     if q.numel() == 0:
         return o, row_sums
@@ -447,6 +517,12 @@ def _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups=1, window_size=0, use_fast_sq
 
 def _sp2norm_flash_bwd(q, k, v, o, do, row_sums, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True):
     """Run the fused backward; return (dq, dk, dv) like kernels.py:1934-1989."""
+    if _tracing(q, k, v, o, do, row_sums):
+        return _ops().flash_bwd(q, k, v, o, do, row_sums, float(scale), int(window_size), bool(use_fast_sqrt))
+    return _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt)
+
+
+def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt):
     B, H_q, T, D = q.shape
     H_kv = k.shape[1]
     do = _flash_ready(do)
@@ -474,7 +550,8 @@ def _sp2norm_flash_bwd(q, k, v, o, do, row_sums, scale, n_kv_groups=1, window_si
 class _SP2NormFlashAttentionFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt):
-        q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
+        if not _tracing(q, k, v):  # the traced op readies its inputs itself
+            q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
         o, row_sums = _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt)
         ctx.save_for_backward(q, k, v, o, row_sums)
         ctx.scale = scale
@@ -610,7 +687,21 @@ def _rope_tables(cos, sin, T, D, device):
 
 def _rope_flash_fwd(q, k, v, cos, sin, scale, window_size, o=None):
     """Rotate q/k (sa_rope_flash_fwd) and run the tcgen05 forward; ``o`` may be
-    a strided view to write into.  Returns (o, row_sums)."""
+    a strided view to write into.  Returns (o, row_sums); row_sums is None
+    under a tracer (the traced op returns o only)."""
+    if _tracing(q, k, v, cos, sin):
+        _flash_check(q, k, v)
+        T, D = q.shape[2], q.shape[3]
+        assert cos.shape == (T, D // 2) and sin.shape == (T, D // 2)
+        res = _ops().rope_flash_fwd(q, k, v, cos, sin, float(scale), int(window_size))
+        if o is None:
+            return res, None
+        o.copy_(res)
+        return o, None
+    return _rope_flash_fwd_direct(q, k, v, cos, sin, scale, window_size, o)
+
+
+def _rope_flash_fwd_direct(q, k, v, cos, sin, scale, window_size, o=None):
     B, H_q, T, D = q.shape
     H_kv = k.shape[1]
     _flash_check(q, k, v)
@@ -720,6 +811,14 @@ def sp2norm_fp8_flash_attention(q, k, v, *, scale=None, window_size=0):
         raise ValueError(f"q/k/v must share one dtype, got {q.dtype}/{k.dtype}/{v.dtype}")
     if D not in FLASH_HEAD_DIMS:
         raise ValueError(f"head dim {D} not supported (supported: {FLASH_HEAD_DIMS})")
+    if _tracing(q, k, v):
+        return _ops().fp8_flash_fwd(q, k, v, float(scale), int(window_size))
+    return _fp8_flash_fwd_direct(q, k, v, scale, window_size)
+
+
+def _fp8_flash_fwd_direct(q, k, v, scale, window_size):
+    B, H_q, T, D = q.shape
+    H_kv = k.shape[1]
     o = torch.empty(B, H_q, T, D, device=q.device, dtype=torch.bfloat16)
     if q.numel() == 0:
         return o
@@ -785,6 +884,15 @@ def sp2norm_paged_attention(q, k_cache, v_cache, block_table, context_lens, *, s
         raise ValueError(f"head dim {D} not supported (supported: {PAGED_HEAD_DIMS})")
     if k_cache.shape != v_cache.shape or k_cache.shape[3] != D:
         raise ValueError(f"k_cache {tuple(k_cache.shape)} / v_cache {tuple(v_cache.shape)} do not match D={D}")
+    if _tracing(q, k_cache, v_cache, block_table, context_lens):
+        return _ops().paged_decode(q, k_cache, v_cache, block_table, context_lens, float(scale), int(block_size))
+    return _paged_decode_direct(q, k_cache, v_cache, block_table, context_lens, scale, block_size)
+
+
+def _paged_decode_direct(q, k_cache, v_cache, block_table, context_lens, scale, block_size):
+    B, H_q, _, D = q.shape
+    H_kv = k_cache.shape[1]
+    max_blocks_per_seq = block_table.shape[1]
     q = q.contiguous()
     k_cache = k_cache.contiguous()
     v_cache = v_cache.contiguous()
