@@ -498,6 +498,24 @@ def extra_decode(shapes, steps, world, g, hbm, O):
         dec[key] = {"us": round(ms * 1e3, 1), "GB/s": _gbs(b, ms), "frac_hbm": round(b / (ms * 1e-3) / 1e9 / hbm, 3),
                     "kv_bytes": b, "inputs_vs_L2": "larger" if b > 126e6 else "smaller (L2-resident, warm)",
                     "kernel": "tcgen05" if (Hq // Hkv >= 2 and D == 128) else "cuda-core"}
+        if B <= 8:
+            # the same call captured once in a CUDA graph and replayed, as a
+            # serving loop would: what is left is the kernels' own latency
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    f()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                f()
+            for _ in range(3):
+                graph.replay()
+            ms_g = time_steps(graph.replay, steps, world) / steps
+            dec[key]["graph_replay_us"] = round(ms_g * 1e3, 1)
+            dec[key]["graph_replay_frac_hbm"] = round(b / (ms_g * 1e-3) / 1e9 / hbm, 3)
+            del graph
         if B == 1 and T == 8192:
             o = f()
             ref = O.paged_decode_attention(q.float().cpu().numpy(), kc.float().cpu().numpy(),
