@@ -11,7 +11,10 @@ without the built library the kernel entry points raise ``RuntimeError``.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import functools
+import os
 import math
 import threading
 from dataclasses import dataclass
@@ -155,7 +158,17 @@ def _finalize_output(kernel_out, user_out):
 
 
 def _stream(t):
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    """torch's current stream on t's device, as the raw handle the C ABI takes
+    (the raw lookup skips building a torch.cuda.Stream per call)."""
+    return ctypes.c_void_p(torch._C._cuda_getCurrentRawStream(t.device.index))
+
+
+def _on(device):
+    """Make ``device`` current for a launch; no guard when it already is
+    (the common case: entering torch.cuda.device costs microseconds per call)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def _is_winner_family(family):
@@ -208,7 +221,7 @@ def _launch_norm_fwd(x2d, out2d, family, causal, rowsum=None):
 def _norm_fwd_direct(x2d, out2d, family, causal, rowsum=None):
     rows, cols = x2d.shape
     _check_cols(cols)
-    with torch.cuda.device(x2d.device):
+    with _on(x2d.device):
         st = _lib.load().sa_norm_fwd(
             x2d.data_ptr(), out2d.data_ptr(), rowsum.data_ptr() if rowsum is not None else None,
             rows, cols, max(x2d.stride(0), cols), max(out2d.stride(0), cols),
@@ -232,7 +245,7 @@ def _launch_norm_bwd(x2d, g2d, rowsum, dx2d, family, causal):
 def _norm_bwd_direct(x2d, g2d, rowsum, dx2d, family, causal):
     rows, cols = x2d.shape
     _check_cols(cols)
-    with torch.cuda.device(x2d.device):
+    with _on(x2d.device):
         st = _lib.load().sa_norm_bwd(
             x2d.data_ptr(), g2d.data_ptr(), rowsum.data_ptr() if rowsum is not None else None, dx2d.data_ptr(),
             rows, cols, max(x2d.stride(0), cols), max(g2d.stride(0), cols), max(dx2d.stride(0), cols),
@@ -505,7 +518,7 @@ def _flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt, o=None):
     row_sums = torch.empty(B, H_q, T, device=q.device, dtype=torch.float32)
     if q.numel() == 0:
         return o, row_sums
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         st = _lib.load().sa_flash_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
             B, H_q, H_kv, T, D, _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o),
@@ -534,7 +547,7 @@ def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqr
     lib = _lib.load()
     ws_bytes = int(lib.sa_flash_bwd_workspace_size(B, H_q, H_kv, T, D))
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         st = lib.sa_flash_bwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), row_sums.data_ptr(),
             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
@@ -610,7 +623,7 @@ def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=
     row_sums = torch.empty(B, H_q, Tq, device=q.device, dtype=torch.float32)
     if q.numel() == 0:
         return o, row_sums
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         st = _lib.load().sa_flash_fwd_chunk(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
             B, H_q, H_kv, Tq, Tk, int(q_offset), D, _lib.strides(q), _lib.strides(k), _lib.strides(v),
@@ -641,7 +654,7 @@ def sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, row_sums, q_offset, *, sca
     lib = _lib.load()
     ws_bytes = int(lib.sa_flash_bwd_workspace_size(B, H_q, H_kv, Tq, D))
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         st = lib.sa_flash_bwd_chunk(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), row_sums.data_ptr(),
             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
@@ -715,7 +728,7 @@ def _rope_flash_fwd_direct(q, k, v, cos, sin, scale, window_size, o=None):
     lib = _lib.load()
     nbytes = lib.sa_rope_flash_fwd_workspace_size(B, H_q, H_kv, T, D)
     ws = torch.empty(nbytes, device=q.device, dtype=torch.uint8)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         st = lib.sa_rope_flash_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
             cos.data_ptr(), sin.data_ptr(), _DTYPE_CODE[cos.dtype], ws.data_ptr(), nbytes,
@@ -781,7 +794,7 @@ def _fp8_quantize(q, k, v):
     vq = torch.empty(v.shape, device=dev, dtype=torch.bfloat16)
     scales = torch.empty(3, device=dev, dtype=torch.float32)
     amax = torch.empty(3, device=dev, dtype=torch.int32)
-    with torch.cuda.device(dev):
+    with _on(dev):
         st = _lib.load().sa_fp8_quantize(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.numel(), k.numel(), v.numel(),
                                          _DTYPE_CODE[q.dtype], q8.data_ptr(), k8.data_ptr(), vq.data_ptr(),
                                          scales.data_ptr(), amax.data_ptr(), _stream(q))
@@ -824,7 +837,7 @@ def _fp8_flash_fwd_direct(q, k, v, scale, window_size):
         return o
     q8, k8, vq, scales = _fp8_quantize(q, k, v)
     row_sums = torch.empty(B, H_q, T, device=q.device, dtype=torch.float32)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         st = _lib.load().sa_fp8_flash_fwd(
             q8.data_ptr(), k8.data_ptr(), vq.data_ptr(), o.data_ptr(), row_sums.data_ptr(), scales.data_ptr(),
             B, H_q, H_kv, T, D, _lib.strides(q8), _lib.strides(k8), _lib.strides(vq), _lib.strides(o),
@@ -841,6 +854,19 @@ def _fp8_flash_fwd_direct(q, k, v, scale, window_size):
 PAGED_HEAD_DIMS = (32, 64, 128, 256)
 _paged_ws = {}  # (device index, stream handle) -> zero-ticketed workspace
 _paged_ws_lock = threading.Lock()
+
+
+def _paged_ws_size(B, H_q, H_kv, max_blocks, block_size, D, dtype_code, device_index):
+    """sa_paged_decode_workspace_size, cached: it depends only on the shape,
+    the device (its SM count) and the kernel choice (SA_PAGED_DECODE_KERNEL),
+    and decode calls repeat one shape."""
+    return _paged_ws_size_cached(B, H_q, H_kv, max_blocks, block_size, D, dtype_code, device_index,
+                                 os.environ.get("SA_PAGED_DECODE_KERNEL"))
+
+
+@functools.lru_cache(maxsize=256)
+def _paged_ws_size_cached(B, H_q, H_kv, max_blocks, block_size, D, dtype_code, device_index, choice):
+    return int(_lib.load().sa_paged_decode_workspace_size(B, H_q, H_kv, max_blocks, block_size, D, dtype_code))
 
 
 def _paged_workspace(device, stream_handle, nbytes):
@@ -904,9 +930,9 @@ def _paged_decode_direct(q, k_cache, v_cache, block_table, context_lens, scale, 
     if max_blocks_per_seq == 0 or k_cache.shape[0] == 0:
         return out.zero_()
     lib = _lib.load()
-    with torch.cuda.device(q.device):
-        nbytes = lib.sa_paged_decode_workspace_size(B, H_q, H_kv, max_blocks_per_seq, block_size, D,
-                                                    _DTYPE_CODE[q.dtype])
+    with _on(q.device):
+        nbytes = _paged_ws_size(B, H_q, H_kv, max_blocks_per_seq, block_size, D, _DTYPE_CODE[q.dtype],
+                                q.device.index)
         if nbytes < 0:
             _lib.check(int(nbytes), "sa_paged_decode_workspace_size")
         stream = _stream(q)
