@@ -680,17 +680,6 @@ def precompute_rope_cos_sin(dim, seq_len, base=10000.0, device="cuda", dtype=tor
     return freqs.cos().to(dtype), freqs.sin().to(dtype)
 
 
-def _not_built(name, ref):
-    def fn(*args, **kwargs):
-        raise NotImplementedError(
-            f"{name} ({ref}) is not part of this build's B200 hot path yet; "
-            "use sp2norm_flash_attention for fused squareplus attention"
-        )
-
-    fn.__name__ = name
-    return fn
-
-
 def _rope_tables(cos, sin, T, D, device):
     assert cos.shape == (T, D // 2) and sin.shape == (T, D // 2)
     if cos.dtype not in _DTYPE_CODE or sin.dtype != cos.dtype:
