@@ -29,7 +29,10 @@ def _capture(fn):
             fn()
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    # thread-local capture: a CUDA call from another thread of the test
+    # process (e.g. a compile worker left by an earlier test) must not
+    # invalidate this capture
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
         out = fn()
     return g, out
 
