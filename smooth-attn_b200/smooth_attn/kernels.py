@@ -175,19 +175,20 @@ def _is_winner_family(family):
     return family.cache_key == DEFAULT_FAMILY.cache_key
 
 
+from torch._subclasses.fake_tensor import FakeTensor as _FakeTensor  # noqa: E402
+from torch._subclasses.functional_tensor import FunctionalTensor as _FunctionalTensor  # noqa: E402
+from torch.fx.experimental.proxy_tensor import get_proxy_mode as _get_proxy_mode  # noqa: E402
+
+_TRACED_TYPES = (_FakeTensor, _FunctionalTensor)
+
+
 def _tracing(*tensors):
     """True under torch.compile / make_fx / export: the kernels must then be
     reached through the torch.library ops in ``_ops.py`` (a ctypes launch
     is not traceable, and fake tensors have no data pointer)."""
-    if torch.compiler.is_compiling():
+    if torch.compiler.is_compiling() or _get_proxy_mode() is not None:
         return True
-    from torch._subclasses.fake_tensor import FakeTensor
-    from torch._subclasses.functional_tensor import FunctionalTensor
-    from torch.fx.experimental.proxy_tensor import get_proxy_mode
-
-    if get_proxy_mode() is not None:
-        return True
-    return any(isinstance(t, (FakeTensor, FunctionalTensor)) for t in tensors)
+    return any(isinstance(t, _TRACED_TYPES) for t in tensors)
 
 
 def _ops():
