@@ -24,6 +24,7 @@ bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -508,8 +509,15 @@ def extra_decode(shapes, steps, world, g, hbm, O):
                     f()
             torch.cuda.current_stream().wait_stream(side)
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                f()
+            # no garbage collection mid-capture (a collected graph would free
+            # its pool and invalidate this capture)
+            gc.collect()
+            gc.disable()
+            try:
+                with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                    f()
+            finally:
+                gc.enable()
             for _ in range(3):
                 graph.replay()
             ms_g = time_steps(graph.replay, steps, world) / steps

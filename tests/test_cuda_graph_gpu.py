@@ -4,6 +4,8 @@ synchronises the host, so it can be captured once and replayed with new
 input data (a serving loop's decode step, a training step's attention).
 Replays must give what an eager call on the same inputs gives."""
 
+import gc
+
 import pytest
 import torch
 
@@ -29,11 +31,20 @@ def _capture(fn):
             fn()
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
-    # thread-local capture: a CUDA call from another thread of the test
-    # process (e.g. a compile worker left by an earlier test) must not
-    # invalidate this capture
-    with torch.cuda.graph(g, capture_error_mode="thread_local"):
-        out = fn()
+    # Garbage from earlier tests (graphs kept alive by reference cycles) must
+    # not be collected mid-capture: destroying a graph frees its memory pool
+    # (cudaFree), which invalidates the capture.  torch.cuda.graph no longer
+    # collects before capturing by default, so collect here and keep the
+    # collector off until the capture ends.  Thread-local mode: a CUDA call
+    # from another thread of the process (a compile worker) must not
+    # invalidate it either.
+    gc.collect()
+    gc.disable()
+    try:
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            out = fn()
+    finally:
+        gc.enable()
     return g, out
 
 
@@ -60,6 +71,7 @@ def test_flash_fwd_bwd_graphed_callable():
     forward and backward graphs, replayed on fresh inputs."""
     shp = [(2, 8, 512, 128), (2, 2, 512, 128), (2, 2, 512, 128)]
     sample = [randn(s, i, torch.bfloat16, CUDA).requires_grad_(True) for i, s in enumerate(shp)]
+    gc.collect()
     fn = torch.cuda.make_graphed_callables(lambda q, k, v: sa.sp2norm_flash_attention(q, k, v, window_size=300),
                                            tuple(sample))
     for step in range(2):
@@ -78,6 +90,7 @@ def test_flash_fwd_bwd_graphed_callable():
 
 def test_norm_graphed_callable():
     x0 = randn((2, 8, 384, 384), 1, torch.bfloat16, CUDA).requires_grad_(True)
+    gc.collect()
     fn = torch.cuda.make_graphed_callables(lambda x: sa.softplus_norm_causal(x), (x0,))
     x = randn(x0.shape, 2, torch.bfloat16, CUDA).requires_grad_(True)
     xr = x.detach().clone().requires_grad_(True)
