@@ -16,6 +16,8 @@ Outputs never alias inputs.  Ops (namespace ``smooth_attn_b200``):
 * ``norm_causal_bwd(x, g, rowsum, alpha, theta, power) -> dx``
 * ``flash_fwd(q, k, v, scale, window_size, use_fast_sqrt) -> (o, row_sums)``
 * ``flash_bwd(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt) -> (dq, dk, dv)``
+* ``flash_fwd_chunk(q, k, v, q_offset, scale, window_size, exact_math) -> (o, row_sums)``
+* ``flash_bwd_chunk(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math) -> (dq, dk, dv)``
 * ``rope_flash_fwd(q, k, v, cos, sin, scale, window_size) -> o``
 * ``fp8_flash_fwd(q, k, v, scale, window_size) -> o``
 * ``paged_decode(q, k_cache, v_cache, block_table, context_lens, scale, block_size) -> out``
@@ -101,6 +103,31 @@ def flash_bwd(q: Tensor, k: Tensor, v: Tensor, o: Tensor, do: Tensor, row_sums: 
 
 @flash_bwd.register_fake
 def _(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt):
+    return tuple(torch.empty(t.shape, device=q.device, dtype=q.dtype) for t in (q, k, v))
+
+
+@torch.library.custom_op(f"{NS}::flash_fwd_chunk", mutates_args=(), device_types="cuda")
+def flash_fwd_chunk(q: Tensor, k: Tensor, v: Tensor, q_offset: int, scale: float, window_size: int,
+                    exact_math: bool) -> tuple[Tensor, Tensor]:
+    return K._flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math)
+
+
+@flash_fwd_chunk.register_fake
+def _(q, k, v, q_offset, scale, window_size, exact_math):
+    B, H, T, _ = q.shape
+    return (torch.empty(q.shape, device=q.device, dtype=q.dtype),
+            torch.empty(B, H, T, device=q.device, dtype=torch.float32))
+
+
+@torch.library.custom_op(f"{NS}::flash_bwd_chunk", mutates_args=(), device_types="cuda")
+def flash_bwd_chunk(q: Tensor, k: Tensor, v: Tensor, o: Tensor, do: Tensor, row_sums: Tensor, q_offset: int,
+                    scale: float, window_size: int, exact_math: bool) -> tuple[Tensor, Tensor, Tensor]:
+    return K._flash_bwd_chunk_direct(q, k, v, o, do, row_sums.contiguous(), q_offset, scale, window_size,
+                                     exact_math)
+
+
+@flash_bwd_chunk.register_fake
+def _(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math):
     return tuple(torch.empty(t.shape, device=q.device, dtype=q.dtype) for t in (q, k, v))
 
 

@@ -619,6 +619,14 @@ def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=
     _flash_check(q, k, v)
     if scale is None:
         scale = 1.0 / math.sqrt(D)
+    if _tracing(q, k, v):
+        return _ops().flash_fwd_chunk(q, k, v, int(q_offset), float(scale), int(window_size), bool(exact_math))
+    return _flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math)
+
+
+def _flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math):
+    B, H_q, Tq, D = q.shape
+    H_kv, Tk = k.shape[1], k.shape[2]
     q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
     o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     row_sums = torch.empty(B, H_q, Tq, device=q.device, dtype=torch.float32)
@@ -642,10 +650,18 @@ def sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, row_sums, q_offset, *, sca
     the query block; dk / dv hold this block's contribution only (the
     context-parallel backward sums them over every rank's query blocks).
     """
-    B, H_q, Tq, D = q.shape
-    H_kv, Tk = k.shape[1], k.shape[2]
+    D = q.shape[3]
     if scale is None:
         scale = 1.0 / math.sqrt(D)
+    if _tracing(q, k, v, o, do, row_sums):
+        return _ops().flash_bwd_chunk(q, k, v, o, do, row_sums, int(q_offset), float(scale), int(window_size),
+                                      bool(exact_math))
+    return _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math)
+
+
+def _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math):
+    B, H_q, Tq, D = q.shape
+    H_kv, Tk = k.shape[1], k.shape[2]
     q, k, v, o, do = (_flash_ready(t) for t in (q, k, v, o, do))
     dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     dk = torch.empty(k.shape, device=q.device, dtype=q.dtype)
@@ -669,7 +685,7 @@ def sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, row_sums, q_offset, *, sca
 
 
 # ---------------------------------------------------------------------------
-# forward-only extensions outside this build's hot path (kernels.py:2093-2829)
+# forward-only entry points: RoPE, FP8, paged decode (kernels.py:2093-2829)
 # ---------------------------------------------------------------------------
 
 

@@ -102,6 +102,20 @@ def test_backward_ops_fake_shapes(fake):
     assert dx.shape == x.shape and dx.dtype == x.dtype
 
 
+def test_chunk_paths_trace(fake):
+    q, k, v = _t(1, 4, 128, 64), _t(1, 2, 384, 64), _t(1, 2, 384, 64)
+
+    def f(q, k, v):
+        o, rs = sa.sp2norm_flash_attention_chunk(q, k, v, 256)
+        return (o, rs) + sa.kernels.sp2norm_flash_attention_chunk_bwd(q, k, v, o, torch.ones_like(o), rs, 256)
+
+    t = _targets(_trace(f, q, k, v))
+    assert "smooth_attn_b200.flash_fwd_chunk.default" in t and "smooth_attn_b200.flash_bwd_chunk.default" in t
+    o, rs, dq, dk, dv = f(q, k, v)
+    assert o.shape == q.shape and rs.shape == (1, 4, 128)
+    assert (dq.shape, dk.shape, dv.shape) == (q.shape, k.shape, v.shape)
+
+
 def test_validation_still_runs_under_tracing(fake):
     q = _t(1, 2, 64, 48)
     with pytest.raises(ValueError):

@@ -92,6 +92,9 @@ def test_opcheck_all_ops():
         (OPS.norm_causal_bwd, (x, randn(x.shape, 8, torch.float32, CUDA), xr, 2.0, 0.5, 2)),
         (OPS.flash_fwd, (q, k, v, 0.125, 0, True)),
         (OPS.flash_bwd, (q, k, v, o, do, rs, 0.125, 0, True)),
+        (OPS.flash_fwd_chunk, (q[:, :, 64:], k, v, 64, 0.125, 0, False)),
+        (OPS.flash_bwd_chunk, (q[:, :, 64:].contiguous(), k, v, o[:, :, 64:].contiguous(), do[:, :, 64:].contiguous(),
+                               rs[:, :, 64:].contiguous(), 64, 0.125, 0, False)),
         (OPS.rope_flash_fwd, (q, k, v, cos, sin, 0.125, 0)),
         (OPS.fp8_flash_fwd, (q, k, v, 0.125, 0)),
         (OPS.paged_decode, (qd, kc, vc, bt, cl, 0.125, 16)),
