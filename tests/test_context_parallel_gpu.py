@@ -7,7 +7,6 @@ backward on zig-zag sequence blocks against the single-GPU autograd."""
 import os
 import socket
 
-import numpy as np
 import pytest
 import torch
 
