@@ -62,6 +62,26 @@ SA_API const char* sa_last_cuda_error(void);
 SA_API int sa_device_status(int reset);
 
 /*
+ * sa_device_status scoped to one stream: synchronises only `stream` (not the
+ * device), then reads and optionally clears the same counters through copies
+ * on that stream.  The counters are per device and shared by all streams, so
+ * a timeout recorded by another stream's kernel shows here too.  (No
+ * reference counterpart.)
+ */
+SA_API int sa_stream_status(void* stream, int reset);
+
+/*
+ * Test hook for the bounded-wait path: launches one warp that waits on an
+ * mbarrier nothing ever arrives on, with a limit of limit_ns (1 ns .. 2 s).
+ * The wait gives up, the timeout is recorded (sa_device_status /
+ * sa_stream_status then return SA_ERR_TIMEOUT until reset) and the kernel
+ * exits normally, writing 1 to the device int `done` (2 had the wait
+ * completed).  It faults nothing and leaves the context usable.  (No
+ * reference counterpart: the reference's kernels have no bounded waits.)
+ */
+SA_API int sa_probe_bounded_wait(int64_t limit_ns, int* done, void* stream);
+
+/*
  * Squareplus normalization forward over rows of length `cols`.
  *   y_j = squareplus(alpha * (x_j - theta))^power,  squareplus(a) = (a + sqrt(a^2+4)) / 2
  *   out_j = y_j / (sum_j y_j + 1e-12)
@@ -108,12 +128,19 @@ SA_API int sa_norm_bwd(const void* x, const void* g, const float* rowsum, void* 
  * and the others multiples of 8 elements (16 B) with 16 B aligned bases.
  * dtype: SA_BF16 or SA_F16.  D in {32, 64, 128}.
  * rowsum: fp32 [B, Hq, T] contiguous, receives R (needed by the backward).
+ * o_lo (nullable, same dtype and strides as o): receives the residual of o's
+ * 16-bit rounding, o_lo = round16(o_fp32 - o).  Pass it to sa_flash_bwd,
+ * which then forms delta = rowsum(dO * (o + o_lo)) from the forward's fp32
+ * output instead of its rounded copy (the rounding of o alone moves dQ / dK
+ * by up to ~1.3x the 2e-2 rel / 1e-2 abs bf16 tolerance).  Training callers
+ * pass it; inference callers pass NULL.
  * exact_math = 0 computes sqrt(u) as u * rsqrt(u) (the reference's default).
  *
  * Replaces: _sp2norm_flash_fwd / _sp2norm_flash_fwd_with_rowsum_kernel
  *             (src/smooth_attn/kernels.py:1912-1931, :1549-1631)
  */
-SA_API int sa_flash_fwd(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B, int64_t Hq,
+SA_API int sa_flash_fwd(const void* q, const void* k, const void* v, void* o, void* o_lo, float* rowsum, int64_t B,
+                 int64_t Hq,
                  int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
                  const int64_t* v_strides, const int64_t* o_strides, float scale, int64_t window_size,
                  int exact_math, int dtype, void* stream);
@@ -131,15 +158,18 @@ SA_API int64_t sa_flash_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, i
  * (dK, dV summed over the query heads of a GQA group).
  * q, o, dout, dq: [B, Hq, T, D]; k, v, dk, dv: [B, Hkv, T, D]; strides as in
  * sa_flash_fwd (dq/dk/dv/dout may have their own strides).
- * rowsum: fp32 [B, Hq, T] from sa_flash_fwd.  workspace: at least
+ * rowsum: fp32 [B, Hq, T] from sa_flash_fwd; o_lo (nullable): the residual
+ * sa_flash_fwd wrote next to o (same strides as o).  workspace: at least
  * sa_flash_bwd_workspace_size() bytes, 256 B aligned, contents undefined on
- * entry.
+ * entry.  sa_flash_bwd_workspace_size() returns 0 for sizes whose byte
+ * count overflows int64; such problems are rejected.
  *
  * Replaces: _sp2norm_flash_bwd, _sp2norm_flash_bwd_dq_kernel,
  *           _sp2norm_flash_bwd_dkv_kernel
  *             (src/smooth_attn/kernels.py:1934-1989, :1680-1784, :1800-1909)
  */
-SA_API int sa_flash_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+SA_API int sa_flash_bwd(const void* q, const void* k, const void* v, const void* o,
+                        const void* o_lo, const void* dout,
                  const float* rowsum, void* dq, void* dk, void* dv, void* workspace, int64_t workspace_bytes,
                  int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides,
                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
@@ -158,12 +188,14 @@ SA_API int sa_flash_bwd(const void* q, const void* k, const void* v, const void*
  * library holds until exit.  Problems whose sa_flash_bwd_workspace_size()
  * exceeds it are rejected with SA_ERR_ARG before anything is launched.
  * The first call on a device looks up the array's device address (make that
- * first call before any stream capture).  All calls share the one array:
+ * first call before any stream capture); the address is cached per device
+ * with its CUDA context and looked up again after a device reset.  All calls share the one array:
  * calls that overlap on the GPU (other streams, other threads) race and give
  * wrong results; serialise them.  Calls no cudaMalloc / cudaFree.
  */
 SA_API int64_t sa_flash_bwd_noalloc_max_bytes(void);
-SA_API int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
+SA_API int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                const void* o_lo, const void* dout,
                                 const float* rowsum, void* dq, void* dk, void* dv, int64_t B, int64_t Hq,
                                 int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides,
                                 const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
@@ -183,7 +215,8 @@ SA_API int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, con
  * cross-rank rescaling is needed.  (No reference counterpart: the reference
  * has no sequence parallelism.)
  */
-SA_API int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B,
+SA_API int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void* o, void* o_lo, float* rowsum,
+                              int64_t B,
                               int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk, int64_t q_offset, int64_t D,
                               const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                               const int64_t* o_strides, float scale, int64_t window_size, int exact_math,
@@ -199,7 +232,8 @@ SA_API int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void*
  * Other arguments as sa_flash_bwd (which is this call with Tq = Tk = T,
  * q_offset = 0).  (No reference counterpart.)
  */
-SA_API int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const void* o, const void* dout,
+SA_API int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const void* o,
+                              const void* o_lo, const void* dout,
                               const float* rowsum, void* dq, void* dk, void* dv, void* workspace,
                               int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk,
                               int64_t q_offset, int64_t D, const int64_t* q_strides, const int64_t* k_strides,

@@ -9,9 +9,9 @@
 //   dQ = dS K;  dK = dS^T Q;  dV = P^T dO   (bf16 operands, fp32 accumulate)
 //
 // B200 design (three launches):
-//   1. flash_bwd_prep: delta = rowsum(dO * O) per query row (fp32) and zero
+//   1. sp2_bwd_prep: delta = rowsum(dO * O) per query row (fp32) and zero
 //      the fp32 dQ accumulator (memory-bound, 16-byte vector loads);
-//   2. flash_bwd_kernel: one CTA per 128-row KV tile of one (batch, kv head),
+//   2. sp2_bwd_kernel: one CTA per 128-row KV tile of one (batch, kv head),
 //      looping over the query heads of its GQA group and the 128-row query
 //      tiles that can see it.  K and V stay resident in shared memory; Q / dO
 //      tiles stream through a 2-stage TMA ring.  Per query tile:
@@ -23,7 +23,7 @@
 //        warps 2..5 (thread = query row): dQ rows -> fp32 vector atomics
 //      dK / dV accumulate in TMEM over the whole loop (GQA heads summed
 //      in-CTA like the reference) and are written once at the end.
-//   3. flash_bwd_dq_convert: dQ accumulator -> dq (bf16/fp16, caller strides).
+//   3. sp2_bwd_dq_convert: dQ accumulator -> dq (bf16/fp16, caller strides).
 // The dS tile in shared memory is laid out once (rows = KV, 64-wide query
 // chunks, 128 B swizzle) and read by two MMAs with two descriptors: as a
 // K-major A for dK and as an MN-major A for dQ.
@@ -34,7 +34,7 @@
 #include "sa_sm100.cuh"
 
 namespace sa {
-namespace flash {
+namespace sqattn {
 
 using namespace sm100;
 
@@ -205,7 +205,7 @@ struct BwdBars {
 
 template <int D, bool BF16, bool EXACT>
 __global__ void __launch_bounds__(192, 1)
-    flash_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+    sp2_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
                      BwdParams p) {
   using C = BwdCfg<D>;
@@ -574,7 +574,7 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
 
 template <bool BF16, bool EXACT>
 __global__ void __launch_bounds__(448, 1)
-    flash_bwd128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+    sp2_bwd128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
                         BwdParams p) {
   using C = Bwd128;
@@ -883,7 +883,8 @@ __global__ void __launch_bounds__(448, 1)
 
 // delta = rowsum(dO * O) (fp32) and dq_acc = 0.  One warp per query row.
 template <typename T, int D>
-__global__ void __launch_bounds__(256) flash_bwd_prep(const T* __restrict__ o, const T* __restrict__ dout,
+__global__ void __launch_bounds__(256) sp2_bwd_prep(const T* __restrict__ o, const T* __restrict__ o_lo,
+                                                    const T* __restrict__ dout,
                                                       float* __restrict__ delta, float* __restrict__ dq_acc,
                                                       int64_t rows, int Hq, int Tlen, int64_t so_b, int64_t so_h,
                                                       int64_t so_s, int64_t sd_b, int64_t sd_h, int64_t sd_s) {
@@ -903,19 +904,25 @@ __global__ void __launch_bounds__(256) flash_bwd_prep(const T* __restrict__ o, c
   for (int64_t r0 = (int64_t)blockIdx.x * RPB + threadIdx.x / LPR; r0 < rows; r0 += 2 * stride) {
     const int64_t r1 = r0 + stride;
     const bool two = r1 < rows;
-    Pack<T, VEC> a0, c0, a1, c1;
+    Pack<T, VEC> a0, c0, a1, c1, l0, l1;
     a0.u = *reinterpret_cast<const uint4*>(addr(r0, o, so_b, so_h, so_s));
     c0.u = *reinterpret_cast<const uint4*>(addr(r0, dout, sd_b, sd_h, sd_s));
     if (two) {
       a1.u = *reinterpret_cast<const uint4*>(addr(r1, o, so_b, so_h, so_s));
       c1.u = *reinterpret_cast<const uint4*>(addr(r1, dout, sd_b, sd_h, sd_s));
     }
+    l0.zero();
+    l1.zero();
+    if (o_lo != nullptr) {  // o + o_lo = the forward's fp32 output to ~16 mantissa bits (exact in fp32)
+      l0.u = *reinterpret_cast<const uint4*>(addr(r0, o_lo, so_b, so_h, so_s));
+      if (two) l1.u = *reinterpret_cast<const uint4*>(addr(r1, o_lo, so_b, so_h, so_s));
+    }
     float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) acc0 += a0.get(e) * c0.get(e);
+    for (int e = 0; e < VEC; ++e) acc0 += (a0.get(e) + l0.get(e)) * c0.get(e);
     if (two) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) acc1 += a1.get(e) * c1.get(e);
+      for (int e = 0; e < VEC; ++e) acc1 += (a1.get(e) + l1.get(e)) * c1.get(e);
     }
 #pragma unroll
     for (int off = LPR / 2; off > 0; off >>= 1) {
@@ -936,7 +943,7 @@ __global__ void __launch_bounds__(256) flash_bwd_prep(const T* __restrict__ o, c
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(256) flash_bwd_dq_convert(const float* __restrict__ dq_acc, T* __restrict__ dq,
+__global__ void __launch_bounds__(256) sp2_bwd_dq_convert(const float* __restrict__ dq_acc, T* __restrict__ dq,
                                                             int64_t rows, int Hq, int Tlen, int64_t s_b, int64_t s_h,
                                                             int64_t s_s) {
   constexpr int VEC = 8;
@@ -957,7 +964,7 @@ __global__ void __launch_bounds__(256) flash_bwd_dq_convert(const float* __restr
 }
 
 template <int D, bool BF16, bool EXACT>
-static int launch_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+static int launch_bwd(const void* q, const void* k, const void* v, const void* o, const void* o_lo, const void* dout,
                       const float* rowsum, void* dq, void* dk, void* dv, float* dq_acc, float* delta, int64_t B,
                       int64_t Hq, int64_t Hkv, int64_t T, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                       const int64_t* os, const int64_t* dos, const int64_t* dqs, const int64_t* dks,
@@ -972,10 +979,10 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
   if (cudaGetDevice(&prep_dev) == cudaSuccess)
     cudaDeviceGetAttribute(&prep_sms, cudaDevAttrMultiProcessorCount, prep_dev);
   const int64_t prep_rpb = 256 / (D / 8);
-  flash_bwd_prep<T16, D><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + prep_rpb - 1) / prep_rpb,
+  sp2_bwd_prep<T16, D><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + prep_rpb - 1) / prep_rpb,
                                                                               (int64_t)prep_sms * 8)),
                            256, 0, st>>>(
-      static_cast<const T16*>(o), static_cast<const T16*>(dout), delta, dq_acc, rows, (int)Hq, (int)T, os[0], os[1],
+      static_cast<const T16*>(o), static_cast<const T16*>(o_lo), static_cast<const T16*>(dout), delta, dq_acc, rows, (int)Hq, (int)T, os[0], os[1],
       os[2], dos[0], dos[1], dos[2]);
   CUtensorMap mq, mk, mv, mdo;
   if (!make_map_4d(&mq, q, BF16, B, Hq, T, D, qs, C::CHUNK, C::BQ) ||
@@ -1005,28 +1012,30 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
     if (!make_map_4d(&mq64, q, BF16, B, Hq, T, D, qs, 64, Bwd128::BQ) ||
         !make_map_4d(&mdo64, dout, BF16, B, Hq, T, D, dos, 64, Bwd128::BQ))
       return SA_ERR_ALIGN;
-    auto kern = flash_bwd128_kernel<BF16, EXACT>;
+    auto kern = sp2_bwd128_kernel<BF16, EXACT>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Bwd128::SMEM);
     kern<<<grid, Bwd128::THREADS, Bwd128::SMEM, st>>>(mq64, mk, mv, mdo64, p);
   } else {
-    auto kern = flash_bwd_kernel<D, BF16, EXACT>;
+    auto kern = sp2_bwd_kernel<D, BF16, EXACT>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     kern<<<grid, 192, C::SMEM, st>>>(mq, mk, mv, mdo, p);
   }
   const int64_t nthreads = rows * (D / 8);
-  flash_bwd_dq_convert<T16, D><<<(unsigned)((nthreads + 255) / 256), 256, 0, st>>>(
+  sp2_bwd_dq_convert<T16, D><<<(unsigned)((nthreads + 255) / 256), 256, 0, st>>>(
       dq_acc, static_cast<T16*>(dq), rows, (int)Hq, (int)T, dqs[0], dqs[1], dqs[2]);
   return SA_OK;
 }
 
-}  // namespace flash
+}  // namespace sqattn
 
-int flash_bwd_timeouts(int reset) {
+int flash_bwd_timeouts(int reset, cudaStream_t st) {
   unsigned v = 0;
-  cudaMemcpyFromSymbol(&v, flash::g_flash_bwd_timeouts, sizeof(v));
+  cudaMemcpyFromSymbolAsync(&v, sqattn::g_flash_bwd_timeouts, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
   if (reset) {
     const unsigned z = 0;
-    cudaMemcpyToSymbol(flash::g_flash_bwd_timeouts, &z, sizeof(z));
+    cudaMemcpyToSymbolAsync(sqattn::g_flash_bwd_timeouts, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
   }
   return (int)v;
 }
@@ -1042,13 +1051,22 @@ static bool bwd_strides_ok(const int64_t* s) {
 
 static int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
 
+// 0 for empty problems and for sizes whose byte count does not fit in an
+// int64 (every product below is checked before it is formed).
 extern "C" int64_t sa_flash_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D) {
   (void)Hkv;
   if (B <= 0 || Hq <= 0 || T <= 0 || D <= 0) return 0;
-  return align256(B * Hq * T * D * 4) + align256(B * Hq * T * 4);
+  int64_t rows, elems, acc_bytes, total;
+  if (__builtin_mul_overflow(B, Hq, &rows) || __builtin_mul_overflow(rows, T, &rows) ||
+      __builtin_mul_overflow(rows, D, &elems) || __builtin_mul_overflow(elems, (int64_t)4, &acc_bytes) ||
+      acc_bytes > INT64_MAX / 2 - 1024)
+    return 0;
+  total = align256(acc_bytes) + align256(rows * 4);
+  return total;
 }
 
-extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const void* o,
+                            const void* o_lo, const void* dout,
                             const float* rowsum, void* dq, void* dk, void* dv, void* workspace,
                             int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D,
                             const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
@@ -1059,23 +1077,25 @@ extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const v
   if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
   if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Hq % Hkv != 0 || window_size < 0) return SA_ERR_ARG;
   if (B == 0 || T == 0) return SA_OK;
-  if (T > (1ll << 30) || B * Hkv > 65535) return SA_ERR_UNSUPPORTED;
+  if (T > (1ll << 30) || B > INT32_MAX || Hq > INT32_MAX || B * Hq > INT32_MAX ||
+      sa_flash_bwd_workspace_size(B, Hq, Hkv, T, D) <= 0)
+    return SA_ERR_UNSUPPORTED;
   if (!q || !k || !v || !o || !dout || !rowsum || !dq || !dk || !dv || !workspace) return SA_ERR_ARG;
   if (workspace_bytes < sa_flash_bwd_workspace_size(B, Hq, Hkv, T, D)) return SA_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_ALIGN;
   const int64_t* all[8] = {q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides};
   for (auto s : all)
     if (!bwd_strides_ok(s)) return SA_ERR_ALIGN;
-  const void* ptrs[9] = {q, k, v, o, dout, dq, dk, dv, rowsum};
+  const void* ptrs[10] = {q, k, v, o, o_lo, dout, dq, dk, dv, rowsum};
   for (auto p : ptrs)
     if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return SA_ERR_ALIGN;
   float* dq_acc = static_cast<float*>(workspace);
   float* delta = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(B * Hq * T * D * 4));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  using namespace sa::flash;
+  using namespace sa::sqattn;
   int rc;
 #define SA_BWD_CASE(DD, BF, EX)                                                                                  \
-  rc = launch_bwd<DD, BF, EX>(q, k, v, o, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, T, q_strides,     \
+  rc = launch_bwd<DD, BF, EX>(q, k, v, o, o_lo, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, T, q_strides,     \
                               k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, \
                               scale, window_size, st)
 #define SA_BWD_D(DD)                              \
@@ -1099,7 +1119,8 @@ extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const v
   return sa_record_cuda_error(cudaGetLastError());
 }
 
-extern "C" int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const void* o, const void* dout,
+extern "C" int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const void* o,
+                                  const void* o_lo, const void* dout,
                                   const float* rowsum, void* dq, void* dk, void* dv, void* workspace,
                                   int64_t workspace_bytes, int64_t B, int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk,
                                   int64_t q_offset, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
@@ -1111,23 +1132,25 @@ extern "C" int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, c
   if (B < 0 || Hq < 1 || Hkv < 1 || Tq < 0 || Tk < 0 || q_offset < 0 || Hq % Hkv != 0 || window_size < 0)
     return SA_ERR_ARG;
   if (B == 0 || Tq == 0 || Tk == 0) return Tk == 0 && Tq > 0 ? SA_ERR_ARG : SA_OK;
-  if (Tq > (1ll << 30) || Tk > (1ll << 30) || q_offset > (1ll << 30) || B * Hkv > 65535) return SA_ERR_UNSUPPORTED;
+  if (Tq > (1ll << 30) || Tk > (1ll << 30) || q_offset > (1ll << 30) || B > INT32_MAX || Hq > INT32_MAX ||
+      B * Hq > INT32_MAX || sa_flash_bwd_workspace_size(B, Hq, Hkv, Tq, D) <= 0)
+    return SA_ERR_UNSUPPORTED;
   if (!q || !k || !v || !o || !dout || !rowsum || !dq || !dk || !dv || !workspace) return SA_ERR_ARG;
   if (workspace_bytes < sa_flash_bwd_workspace_size(B, Hq, Hkv, Tq, D)) return SA_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SA_ERR_ALIGN;
   const int64_t* all[8] = {q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides};
   for (auto s : all)
     if (!bwd_strides_ok(s)) return SA_ERR_ALIGN;
-  const void* ptrs[9] = {q, k, v, o, dout, dq, dk, dv, rowsum};
+  const void* ptrs[10] = {q, k, v, o, o_lo, dout, dq, dk, dv, rowsum};
   for (auto p : ptrs)
     if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return SA_ERR_ALIGN;
   float* dq_acc = static_cast<float*>(workspace);
   float* delta = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(B * Hq * Tq * D * 4));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  using namespace sa::flash;
+  using namespace sa::sqattn;
   int rc;
 #define SA_BWDC_CASE(DD, BF, EX)                                                                                 \
-  rc = launch_bwd<DD, BF, EX>(q, k, v, o, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, Tq, q_strides,   \
+  rc = launch_bwd<DD, BF, EX>(q, k, v, o, o_lo, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, Tq, q_strides,   \
                               k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, \
                               scale, window_size, st, Tk, q_offset)
 #define SA_BWDC_D(DD)                              \
@@ -1172,28 +1195,49 @@ static __device__ __align__(256) unsigned char g_bwd_noalloc_scratch[SA_NOALLOC_
 
 // Device address of the scratch array for the current device.  In host code
 // the array's name is only a host-side handle; the real device address is
-// looked up once per device (with that device current) and cached.
+// looked up once per device (with that device current) and cached together
+// with the CUDA context it belongs to.  A device reset or a new primary
+// context reloads the module, possibly at another address, so a cached entry
+// whose context is no longer the current one is looked up again.
 static int noalloc_scratch(void** out) {
+  using CtxGetCurrent = CUresult (*)(CUcontext*);
+  static CtxGetCurrent ctx_get = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      ctx_get = reinterpret_cast<CtxGetCurrent>(fn);
+  });
   static std::mutex mu;
   static void* addr[64] = {nullptr};
+  static CUcontext ctx[64] = {nullptr};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return sa_record_cuda_error(e);
   if (dev < 0 || dev >= 64) return SA_ERR_UNSUPPORTED;
+  CUcontext cur = nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) return sa_record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-    addr[dev] = p;
+  if (addr[dev] != nullptr && ctx_get != nullptr && ctx_get(&cur) == CUDA_SUCCESS && cur == ctx[dev]) {
+    *out = addr[dev];
+    return SA_OK;
   }
-  *out = addr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) return sa_record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+  cur = nullptr;
+  if (ctx_get != nullptr && ctx_get(&cur) != CUDA_SUCCESS) cur = nullptr;
+  addr[dev] = p;
+  ctx[dev] = cur;
+  *out = p;
   return SA_OK;
 }
 
 extern "C" int64_t sa_flash_bwd_noalloc_max_bytes(void) { return SA_NOALLOC_SCRATCH_BYTES; }
 
-extern "C" int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
+extern "C" int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                    const void* o_lo, const void* dout,
                                     const float* rowsum, void* dq, void* dk, void* dv, int64_t B, int64_t Hq,
                                     int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides,
                                     const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
@@ -1201,13 +1245,14 @@ extern "C" int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v,
                                     const int64_t* dv_strides, float scale, int64_t window_size, int exact_math,
                                     int dtype, void* stream) {
   const int64_t need = sa_flash_bwd_workspace_size(B, Hq, Hkv, T, D);
-  if (need > SA_NOALLOC_SCRATCH_BYTES) return SA_ERR_ARG;  // problem too large for the fixed scratch
+  // too large for the fixed scratch, or so large that the size overflows (0)
+  if (need > SA_NOALLOC_SCRATCH_BYTES || (need == 0 && B > 0 && Hq > 0 && T > 0 && D > 0)) return SA_ERR_ARG;
   void* scratch = nullptr;
   if (need > 0) {
     const int rc = noalloc_scratch(&scratch);
     if (rc != SA_OK) return rc;
   }
-  return sa_flash_bwd(q, k, v, o, dout, rowsum, dq, dk, dv, scratch, SA_NOALLOC_SCRATCH_BYTES, B, Hq, Hkv, T, D,
+  return sa_flash_bwd(q, k, v, o, o_lo, dout, rowsum, dq, dk, dv, scratch, SA_NOALLOC_SCRATCH_BYTES, B, Hq, Hkv, T, D,
                       q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides,
                       scale, window_size, exact_math, dtype, stream);
 }

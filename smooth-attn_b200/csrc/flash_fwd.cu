@@ -31,7 +31,7 @@
 #include "sa_sm100.cuh"
 
 namespace sa {
-namespace flash {
+namespace sqattn {
 
 using namespace sm100;
 
@@ -69,6 +69,7 @@ struct FwdCfg {
 
 struct FwdParams {
   void* o;
+  void* o_lo;  // optional (nullptr): bf16/f16 residual o_f32 - o, same strides as o
   float* rowsum;
   int64_t so_b, so_h, so_s;
   int B, Hq, Hkv, T, npairs, window;
@@ -181,7 +182,7 @@ __device__ __forceinline__ float squareplus_row(uint32_t tS, float scale2, int k
 
 template <int D, bool BF16, bool EXACT, bool QK8 = false>
 __global__ void __launch_bounds__(320, 1)
-    flash_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+    sp2_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, FwdParams p) {
   using C = FwdCfg<D, QK8>;
   static_assert(!QK8 || BF16, "the FP8 forward keeps V and P in bf16");
@@ -399,6 +400,28 @@ __global__ void __launch_bounds__(320, 1)
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
 #pragma unroll
           for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          if (p.o_lo != nullptr) {
+            // residual of the 16-bit rounding: o_hi + o_lo carries ~16 mantissa
+            // bits of the fp32 output, so the backward's delta = dO . o is not
+            // limited by the output's own rounding
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float lo = __uint_as_float(r[e]) * inv, hi = __uint_as_float(r[e + 1]) * inv;
+              float rl, rh;
+              if (BF16) {
+                rl = __uint_as_float(pk[e / 2] << 16);
+                rh = __uint_as_float(pk[e / 2] & 0xffff0000u);
+              } else {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pk[e / 2]));
+                rl = f.x;
+                rh = f.y;
+              }
+              pk[e / 2] = BF16 ? pack2_bf16(lo - rl, hi - rh) : pack2_f16(lo - rl, hi - rh);
+            }
+            uint4* dlo = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.o_lo) + (orow - static_cast<uint8_t*>(p.o)) + c * 64);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) dlo[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
         }
       }
       if (live) p.rowsum[((int64_t)b * p.Hq + h) * p.T + q] = 0.25f * rsum;
@@ -453,7 +476,7 @@ bool make_map_4d(CUtensorMap* map, const void* base, bool bf16, int64_t B, int64
 }
 
 template <int D, bool BF16, bool EXACT, bool QK8 = false>
-static int launch_fwd(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B, int64_t Hq,
+static int launch_fwd(const void* q, const void* k, const void* v, void* o, void* o_lo, float* rowsum, int64_t B, int64_t Hq,
                       int64_t Hkv, int64_t T, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                       const int64_t* os, float scale, int64_t window, cudaStream_t st,
                       const float* dscale = nullptr, int64_t Tk = -1, int64_t qoff = 0) {
@@ -466,6 +489,7 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, floa
     return SA_ERR_ALIGN;
   FwdParams p;
   p.o = o;
+  p.o_lo = o_lo;
   p.rowsum = rowsum;
   p.so_b = os[0];
   p.so_h = os[1];
@@ -480,7 +504,7 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, floa
   p.window = (int)window;
   p.scale2 = 2.0f * scale;
   p.dscale = dscale;
-  auto kern = flash_fwd_kernel<D, BF16, EXACT, QK8>;
+  auto kern = sp2_fwd_kernel<D, BF16, EXACT, QK8>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if ((int64_t)p.npairs * B * Hq > INT32_MAX) return SA_ERR_UNSUPPORTED;  // 1-D grid of (pair, head) CTAs
   dim3 grid((unsigned)(p.npairs * B * Hq));
@@ -488,14 +512,16 @@ static int launch_fwd(const void* q, const void* k, const void* v, void* o, floa
   return SA_OK;
 }
 
-}  // namespace flash
+}  // namespace sqattn
 
-int flash_timeouts(int reset) {
+int flash_timeouts(int reset, cudaStream_t st) {
   unsigned v = 0;
-  cudaMemcpyFromSymbol(&v, flash::g_flash_timeouts, sizeof(v));
+  cudaMemcpyFromSymbolAsync(&v, sqattn::g_flash_timeouts, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
   if (reset) {
     const unsigned z = 0;
-    cudaMemcpyToSymbol(flash::g_flash_timeouts, &z, sizeof(z));
+    cudaMemcpyToSymbolAsync(sqattn::g_flash_timeouts, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
   }
   return (int)v;
 }
@@ -511,7 +537,7 @@ static bool strides_ok(const int64_t* s) {
 
 static bool ptr16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-extern "C" int sa_flash_fwd(const void* q, const void* k, const void* v, void* o, float* rowsum, int64_t B,
+extern "C" int sa_flash_fwd(const void* q, const void* k, const void* v, void* o, void* o_lo, float* rowsum, int64_t B,
                             int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const int64_t* q_strides,
                             const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
                             float scale, int64_t window_size, int exact_math, int dtype, void* stream) {
@@ -519,17 +545,16 @@ extern "C" int sa_flash_fwd(const void* q, const void* k, const void* v, void* o
   if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
   if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Hq % Hkv != 0 || window_size < 0) return SA_ERR_ARG;
   if (B == 0 || T == 0) return SA_OK;
-  if (T > (1ll << 30) || B * Hq > 65535ll * 32768) return SA_ERR_UNSUPPORTED;
+  if (T > (1ll << 30) || B > INT32_MAX || Hq > INT32_MAX || B * Hq > INT32_MAX) return SA_ERR_UNSUPPORTED;
   if (!q || !k || !v || !o || !rowsum) return SA_ERR_ARG;
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides) || !strides_ok(o_strides))
     return SA_ERR_ALIGN;
-  if (!ptr16(q) || !ptr16(k) || !ptr16(v) || !ptr16(o)) return SA_ERR_ALIGN;
-  if (B * Hq > 65535) return SA_ERR_UNSUPPORTED;  // grid.y limit
+  if (!ptr16(q) || !ptr16(k) || !ptr16(v) || !ptr16(o) || !ptr16(o_lo)) return SA_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  using namespace sa::flash;
+  using namespace sa::sqattn;
   int rc;
 #define SA_FWD_CASE(DD, BF, EX) \
-  rc = launch_fwd<DD, BF, EX>(q, k, v, o, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides, o_strides, scale, window_size, st)
+  rc = launch_fwd<DD, BF, EX>(q, k, v, o, o_lo, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides, o_strides, scale, window_size, st)
 #define SA_FWD_D(DD)                                    \
   if (dtype == SA_BF16) {                               \
     if (exact_math) SA_FWD_CASE(DD, true, true);        \
@@ -551,7 +576,7 @@ extern "C" int sa_flash_fwd(const void* q, const void* k, const void* v, void* o
   return sa_record_cuda_error(cudaGetLastError());
 }
 
-extern "C" int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void* o, float* rowsum,
+extern "C" int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, void* o, void* o_lo, float* rowsum,
                                   int64_t B, int64_t Hq, int64_t Hkv, int64_t Tq, int64_t Tk, int64_t q_offset,
                                   int64_t D, const int64_t* q_strides, const int64_t* k_strides,
                                   const int64_t* v_strides, const int64_t* o_strides, float scale,
@@ -562,16 +587,18 @@ extern "C" int sa_flash_fwd_chunk(const void* q, const void* k, const void* v, v
     return SA_ERR_ARG;
   if (B == 0 || Tq == 0) return SA_OK;
   if (Tk == 0) return SA_ERR_ARG;  // every query must see at least one key
-  if (Tq > (1ll << 30) || Tk > (1ll << 30) || q_offset > (1ll << 30) || B * Hq > 65535) return SA_ERR_UNSUPPORTED;
+  if (Tq > (1ll << 30) || Tk > (1ll << 30) || q_offset > (1ll << 30) || B > INT32_MAX || Hq > INT32_MAX ||
+      B * Hq > INT32_MAX)
+    return SA_ERR_UNSUPPORTED;
   if (!q || !k || !v || !o || !rowsum) return SA_ERR_ARG;
   if (!strides_ok(q_strides) || !strides_ok(k_strides) || !strides_ok(v_strides) || !strides_ok(o_strides))
     return SA_ERR_ALIGN;
-  if (!ptr16(q) || !ptr16(k) || !ptr16(v) || !ptr16(o)) return SA_ERR_ALIGN;
+  if (!ptr16(q) || !ptr16(k) || !ptr16(v) || !ptr16(o) || !ptr16(o_lo)) return SA_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  using namespace sa::flash;
+  using namespace sa::sqattn;
   int rc;
 #define SA_FWDC_CASE(DD, BF, EX)                                                                                  \
-  rc = launch_fwd<DD, BF, EX>(q, k, v, o, rowsum, B, Hq, Hkv, Tq, q_strides, k_strides, v_strides, o_strides, \
+  rc = launch_fwd<DD, BF, EX>(q, k, v, o, o_lo, rowsum, B, Hq, Hkv, Tq, q_strides, k_strides, v_strides, o_strides, \
                               scale, window_size, st, nullptr, Tk, q_offset)
 #define SA_FWDC_D(DD)                                   \
   if (dtype == SA_BF16) {                               \
@@ -601,7 +628,7 @@ extern "C" int sa_fp8_flash_fwd(const void* q8, const void* k8, const void* vq, 
   if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
   if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Hq % Hkv != 0 || window_size < 0) return SA_ERR_ARG;
   if (B == 0 || T == 0) return SA_OK;
-  if (T > (1ll << 30) || B * Hq > 65535) return SA_ERR_UNSUPPORTED;
+  if (T > (1ll << 30) || B > INT32_MAX || Hq > INT32_MAX || B * Hq > INT32_MAX) return SA_ERR_UNSUPPORTED;
   if (!q8 || !k8 || !vq || !o || !rowsum || !scales) return SA_ERR_ARG;
   auto bytes_ok = [](const int64_t* s) {  // 1-byte elements: TMA strides in 16-byte units
     return s != nullptr && s[3] == 1 && s[0] % 16 == 0 && s[1] % 16 == 0 && s[2] % 16 == 0 && s[0] >= 0 &&
@@ -612,16 +639,16 @@ extern "C" int sa_fp8_flash_fwd(const void* q8, const void* k8, const void* vq, 
   if (!ptr16(q8) || !ptr16(k8) || !ptr16(vq) || !ptr16(o) || (reinterpret_cast<uintptr_t>(scales) & 3u))
     return SA_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  using namespace sa::flash;
+  using namespace sa::sqattn;
   int rc;
   if (D == 32)
-    rc = launch_fwd<32, true, false, true>(q8, k8, vq, o, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
+    rc = launch_fwd<32, true, false, true>(q8, k8, vq, o, nullptr, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
                                            o_strides, scale, window_size, st, scales);
   else if (D == 64)
-    rc = launch_fwd<64, true, false, true>(q8, k8, vq, o, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
+    rc = launch_fwd<64, true, false, true>(q8, k8, vq, o, nullptr, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
                                            o_strides, scale, window_size, st, scales);
   else
-    rc = launch_fwd<128, true, false, true>(q8, k8, vq, o, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
+    rc = launch_fwd<128, true, false, true>(q8, k8, vq, o, nullptr, rowsum, B, Hq, Hkv, T, q_strides, k_strides, v_strides,
                                             o_strides, scale, window_size, st, scales);
   if (rc != SA_OK) return rc;
   return sa_record_cuda_error(cudaGetLastError());

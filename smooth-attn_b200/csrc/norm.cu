@@ -740,12 +740,14 @@ static void bwd_bulk_t(bool causal, const void* x, const void* g, const float* r
 #undef SA_BB
 }
 
-int norm_timeouts(int reset) {
+int norm_timeouts(int reset, cudaStream_t st) {
   unsigned v = 0;
-  cudaMemcpyFromSymbol(&v, g_norm_timeouts, sizeof(v));
+  cudaMemcpyFromSymbolAsync(&v, g_norm_timeouts, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
   if (reset) {
     const unsigned z = 0;
-    cudaMemcpyToSymbol(g_norm_timeouts, &z, sizeof(z));
+    cudaMemcpyToSymbolAsync(g_norm_timeouts, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
   }
   return (int)v;
 }

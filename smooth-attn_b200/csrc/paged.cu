@@ -430,22 +430,26 @@ __global__ void __launch_bounds__(kPgWarps * 32) paged_decode_kernel(const Paged
   }
 }
 
-int paged_timeouts(int reset) {
+int paged_timeouts(int reset, cudaStream_t st) {
   unsigned t = 0;
-  cudaMemcpyFromSymbol(&t, g_paged_timeouts, sizeof(t));
+  cudaMemcpyFromSymbolAsync(&t, g_paged_timeouts, sizeof(t), 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
   if (reset) {
     const unsigned z = 0;
-    cudaMemcpyToSymbol(g_paged_timeouts, &z, sizeof(z));
+    cudaMemcpyToSymbolAsync(g_paged_timeouts, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
   }
   return (int)t;
 }
 
-int paged_bad_pages(int reset) {
+int paged_bad_pages(int reset, cudaStream_t st) {
   unsigned bad = 0;
-  cudaMemcpyFromSymbol(&bad, g_paged_bad_pages, sizeof(bad));
+  cudaMemcpyFromSymbolAsync(&bad, g_paged_bad_pages, sizeof(bad), 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
   if (reset) {
     const unsigned z = 0;
-    cudaMemcpyToSymbol(g_paged_bad_pages, &z, sizeof(z));
+    cudaMemcpyToSymbolAsync(g_paged_bad_pages, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
   }
   return (int)bad;
 }

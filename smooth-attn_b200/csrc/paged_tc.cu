@@ -40,7 +40,7 @@
 int sa_record_cuda_error(cudaError_t e);
 
 namespace sa {
-namespace flash {
+namespace sqattn {
 bool make_map_4d(CUtensorMap* map, const void* base, bool bf16, int64_t B, int64_t H, int64_t T, int64_t D,
                  const int64_t* strides, int chunk, int rows, bool u8 = false);
 }
@@ -527,22 +527,26 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---- host side ---------------------------------------------------------------
 
-int paged_tc_timeouts(int reset) {
+int paged_tc_timeouts(int reset, cudaStream_t st) {
   unsigned t = 0;
-  cudaMemcpyFromSymbol(&t, ptc::g_ptc_timeouts, sizeof(t));
+  cudaMemcpyFromSymbolAsync(&t, ptc::g_ptc_timeouts, sizeof(t), 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
   if (reset) {
     const unsigned z = 0;
-    cudaMemcpyToSymbol(ptc::g_ptc_timeouts, &z, sizeof(z));
+    cudaMemcpyToSymbolAsync(ptc::g_ptc_timeouts, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
   }
   return (int)t;
 }
 
-int paged_tc_bad_pages(int reset) {
+int paged_tc_bad_pages(int reset, cudaStream_t st) {
   unsigned t = 0;
-  cudaMemcpyFromSymbol(&t, ptc::g_ptc_bad_pages, sizeof(t));
+  cudaMemcpyFromSymbolAsync(&t, ptc::g_ptc_bad_pages, sizeof(t), 0, cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
   if (reset) {
     const unsigned z = 0;
-    cudaMemcpyToSymbol(ptc::g_ptc_bad_pages, &z, sizeof(z));
+    cudaMemcpyToSymbolAsync(ptc::g_ptc_bad_pages, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
   }
   return (int)t;
 }
@@ -576,8 +580,8 @@ int paged_tc_launch(const void* q, const void* k_cache, const void* v_cache, voi
   using namespace ptc;
   CUtensorMap mk, mv;
   const int64_t strides[4] = {Hkv * bs * D, bs * D, D, 1};
-  if (!flash::make_map_4d(&mk, k_cache, true, num_blocks, Hkv, bs, D, strides, 64, (int)bs) ||
-      !flash::make_map_4d(&mv, v_cache, true, num_blocks, Hkv, bs, D, strides, 64, (int)bs))
+  if (!sqattn::make_map_4d(&mk, k_cache, true, num_blocks, Hkv, bs, D, strides, 64, (int)bs) ||
+      !sqattn::make_map_4d(&mv, v_cache, true, num_blocks, Hkv, bs, D, strides, 64, (int)bs))
     return SA_ERR_ALIGN;
   Args a;
   a.q = static_cast<const __nv_bfloat16*>(q);

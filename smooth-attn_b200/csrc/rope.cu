@@ -173,6 +173,6 @@ extern "C" int sa_rope_flash_fwd(const void* q, const void* k, const void* v, vo
   if (rc != SA_OK) return rc;
   const int64_t qs[4] = {Hq * T * D, T * D, D, 1};
   const int64_t ks[4] = {Hkv * T * D, T * D, D, 1};
-  return sa_flash_fwd(qr, kr, v, o, rowsum, B, Hq, Hkv, T, D, qs, ks, v_strides, o_strides, scale, window_size,
+  return sa_flash_fwd(qr, kr, v, o, nullptr, rowsum, B, Hq, Hkv, T, D, qs, ks, v_strides, o_strides, scale, window_size,
                       exact_math, dtype, stream);
 }

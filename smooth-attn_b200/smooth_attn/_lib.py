@@ -36,23 +36,25 @@ SIGNATURES = {
     "sa_status_string": (ctypes.c_char_p, [_int]),
     "sa_last_cuda_error": (ctypes.c_char_p, []),
     "sa_device_status": (_int, [_int]),
+    "sa_stream_status": (_int, [_p, _int]),
+    "sa_probe_bounded_wait": (_int, [_i64, _p, _p]),
     "sa_norm_fwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _int, _int, _f, _f, _int, _p]),
     "sa_norm_bwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _f, _f, _int, _p]),
-    "sa_flash_fwd": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+    "sa_flash_fwd": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
                             _i64p, _i64p, _i64p, _i64p, _f, _i64, _int, _int, _p]),
     "sa_flash_bwd_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),
     "sa_flash_bwd_noalloc_max_bytes": (_i64, []),
-    "sa_flash_bwd_noalloc": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p,
+    "sa_flash_bwd_noalloc": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                     _i64, _i64, _i64, _i64, _i64,
                                     _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
                                     _f, _i64, _int, _int, _p]),
-    "sa_flash_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+    "sa_flash_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
                             _i64, _i64, _i64, _i64, _i64,
                             _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
                             _f, _i64, _int, _int, _p]),
-    "sa_flash_fwd_chunk": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+    "sa_flash_fwd_chunk": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                   _i64p, _i64p, _i64p, _i64p, _f, _i64, _int, _int, _p]),
-    "sa_flash_bwd_chunk": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+    "sa_flash_bwd_chunk": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
                                   _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                   _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
                                   _f, _i64, _int, _int, _p]),

@@ -14,10 +14,13 @@ Outputs never alias inputs.  Ops (namespace ``smooth_attn_b200``):
 
 * ``norm_fwd(x, alpha, theta, power, causal, with_rowsum) -> (out, rowsum)``
 * ``norm_causal_bwd(x, g, rowsum, alpha, theta, power) -> dx``
-* ``flash_fwd(q, k, v, scale, window_size, use_fast_sqrt) -> (o, row_sums)``
-* ``flash_bwd(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt) -> (dq, dk, dv)``
-* ``flash_fwd_chunk(q, k, v, q_offset, scale, window_size, exact_math) -> (o, row_sums)``
-* ``flash_bwd_chunk(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math) -> (dq, dk, dv)``
+* ``flash_fwd(q, k, v, scale, window_size, use_fast_sqrt, with_residual) -> (o, row_sums, o_lo)``
+* ``flash_bwd(q, k, v, o, o_lo, do, row_sums, scale, window_size, use_fast_sqrt) -> (dq, dk, dv)``
+* ``flash_fwd_chunk(q, k, v, q_offset, scale, window_size, exact_math, with_residual) -> (o, row_sums, o_lo)``
+* ``flash_bwd_chunk(q, k, v, o, o_lo, do, row_sums, q_offset, scale, window_size, exact_math) -> (dq, dk, dv)``
+
+``o_lo`` is the residual of o's 16-bit rounding (empty when not requested);
+the backward ops take an empty ``o_lo`` for "none".
 * ``rope_flash_fwd(q, k, v, cos, sin, scale, window_size) -> o``
 * ``fp8_flash_fwd(q, k, v, scale, window_size) -> o``
 * ``paged_decode(q, k_cache, v_cache, block_table, context_lens, scale, block_size) -> out``
@@ -81,53 +84,58 @@ def _(x, g, rowsum, alpha, theta, power):
 
 @torch.library.custom_op(f"{NS}::flash_fwd", mutates_args=(), device_types="cuda")
 def flash_fwd(q: Tensor, k: Tensor, v: Tensor, scale: float, window_size: int,
-              use_fast_sqrt: bool) -> tuple[Tensor, Tensor]:
+              use_fast_sqrt: bool, with_residual: bool) -> tuple[Tensor, Tensor, Tensor]:
     q, k, v = K._flash_ready(q), K._flash_ready(k), K._flash_ready(v)
     o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
-    return K._flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt, o=o)
+    res = K._flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt, o=o, with_residual=with_residual)
+    return res if with_residual else (res[0], res[1], q.new_empty(0))
 
 
 @flash_fwd.register_fake
-def _(q, k, v, scale, window_size, use_fast_sqrt):
+def _(q, k, v, scale, window_size, use_fast_sqrt, with_residual):
     B, H, T, _ = q.shape
     return (torch.empty(q.shape, device=q.device, dtype=q.dtype),
-            torch.empty(B, H, T, device=q.device, dtype=torch.float32))
+            torch.empty(B, H, T, device=q.device, dtype=torch.float32),
+            torch.empty(q.shape if with_residual else (0,), device=q.device, dtype=q.dtype))
 
 
 @torch.library.custom_op(f"{NS}::flash_bwd", mutates_args=(), device_types="cuda")
-def flash_bwd(q: Tensor, k: Tensor, v: Tensor, o: Tensor, do: Tensor, row_sums: Tensor, scale: float,
+def flash_bwd(q: Tensor, k: Tensor, v: Tensor, o: Tensor, o_lo: Tensor, do: Tensor, row_sums: Tensor, scale: float,
               window_size: int, use_fast_sqrt: bool) -> tuple[Tensor, Tensor, Tensor]:
     q, k, v, o = (K._flash_ready(t) for t in (q, k, v, o))
-    return K._flash_bwd_direct(q, k, v, o, do, row_sums.contiguous(), scale, window_size, use_fast_sqrt)
+    return K._flash_bwd_direct(q, k, v, o, do, row_sums.contiguous(), scale, window_size, use_fast_sqrt,
+                               o_lo=o_lo if o_lo.numel() else None)
 
 
 @flash_bwd.register_fake
-def _(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt):
+def _(q, k, v, o, o_lo, do, row_sums, scale, window_size, use_fast_sqrt):
     return tuple(torch.empty(t.shape, device=q.device, dtype=q.dtype) for t in (q, k, v))
 
 
 @torch.library.custom_op(f"{NS}::flash_fwd_chunk", mutates_args=(), device_types="cuda")
 def flash_fwd_chunk(q: Tensor, k: Tensor, v: Tensor, q_offset: int, scale: float, window_size: int,
-                    exact_math: bool) -> tuple[Tensor, Tensor]:
-    return K._flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math)
+                    exact_math: bool, with_residual: bool) -> tuple[Tensor, Tensor, Tensor]:
+    res = K._flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math, with_residual)
+    return res if with_residual else (res[0], res[1], q.new_empty(0))
 
 
 @flash_fwd_chunk.register_fake
-def _(q, k, v, q_offset, scale, window_size, exact_math):
+def _(q, k, v, q_offset, scale, window_size, exact_math, with_residual):
     B, H, T, _ = q.shape
     return (torch.empty(q.shape, device=q.device, dtype=q.dtype),
-            torch.empty(B, H, T, device=q.device, dtype=torch.float32))
+            torch.empty(B, H, T, device=q.device, dtype=torch.float32),
+            torch.empty(q.shape if with_residual else (0,), device=q.device, dtype=q.dtype))
 
 
 @torch.library.custom_op(f"{NS}::flash_bwd_chunk", mutates_args=(), device_types="cuda")
-def flash_bwd_chunk(q: Tensor, k: Tensor, v: Tensor, o: Tensor, do: Tensor, row_sums: Tensor, q_offset: int,
-                    scale: float, window_size: int, exact_math: bool) -> tuple[Tensor, Tensor, Tensor]:
+def flash_bwd_chunk(q: Tensor, k: Tensor, v: Tensor, o: Tensor, o_lo: Tensor, do: Tensor, row_sums: Tensor,
+                    q_offset: int, scale: float, window_size: int, exact_math: bool) -> tuple[Tensor, Tensor, Tensor]:
     return K._flash_bwd_chunk_direct(q, k, v, o, do, row_sums.contiguous(), q_offset, scale, window_size,
-                                     exact_math)
+                                     exact_math, o_lo if o_lo.numel() else None)
 
 
 @flash_bwd_chunk.register_fake
-def _(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math):
+def _(q, k, v, o, o_lo, do, row_sums, q_offset, scale, window_size, exact_math):
     return tuple(torch.empty(t.shape, device=q.device, dtype=q.dtype) for t in (q, k, v))
 
 

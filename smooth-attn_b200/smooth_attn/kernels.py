@@ -502,44 +502,69 @@ def _flash_check(q, k, v):
         raise ValueError(f"head dim {q.shape[-1]} not supported (supported: {FLASH_HEAD_DIMS})")
 
 
-def _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True):
-    """Run the fused forward; return (o, row_sums) like kernels.py:1912-1931."""
+def _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True, with_residual=False):
+    """Run the fused forward; return (o, row_sums) like kernels.py:1912-1931.
+
+    with_residual=True also returns o_lo, the residual of o's 16-bit rounding
+    (o + o_lo = the kernel's fp32 output to ~16 mantissa bits), which the
+    backward uses for delta = rowsum(dO * o).
+    """
     if _tracing(q, k, v):
-        return _ops().flash_fwd(q, k, v, float(scale), int(window_size), bool(use_fast_sqrt))
-    return _flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt)
+        o, rs, o_lo = _ops().flash_fwd(q, k, v, float(scale), int(window_size), bool(use_fast_sqrt),
+                                       bool(with_residual))
+        return (o, rs, o_lo) if with_residual else (o, rs)
+    return _flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt, with_residual=with_residual)
 
 
-def _flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt, o=None):
+def _flash_fwd_direct(q, k, v, scale, window_size, use_fast_sqrt, o=None, with_residual=False):
     B, H_q, T, D = q.shape
     H_kv = k.shape[1]
     if o is None:
         o = torch.empty_like(q)
         if not (o.stride(3) == 1 and all((s * o.element_size()) % 16 == 0 for s in o.stride()[:3])):
             o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    o_lo = torch.empty_strided(o.shape, o.stride(), device=o.device, dtype=o.dtype) if with_residual else None
     row_sums = torch.empty(B, H_q, T, device=q.device, dtype=torch.float32)
     if q.numel() == 0:
-        return o, row_sums
+        return (o, row_sums, o_lo) if with_residual else (o, row_sums)
     with _on(q.device):
         st = _lib.load().sa_flash_fwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), _ptr(o_lo), row_sums.data_ptr(),
             B, H_q, H_kv, T, D, _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o),
             float(scale), int(window_size), int(not use_fast_sqrt), _DTYPE_CODE[q.dtype], _stream(q),
         )
     _lib.check(st, "sa_flash_fwd")
-    return o, row_sums
+    return (o, row_sums, o_lo) if with_residual else (o, row_sums)
 
 
-def _sp2norm_flash_bwd(q, k, v, o, do, row_sums, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True):
-    """Run the fused backward; return (dq, dk, dv) like kernels.py:1934-1989."""
+def _ptr(t):
+    """Device pointer of an optional tensor (None or empty -> NULL)."""
+    return t.data_ptr() if t is not None and t.numel() else None
+
+
+def _match_strides(o_lo, o):
+    """The C ABI reads o_lo with o's strides: copy it into that layout if needed."""
+    if o_lo is None or not o_lo.numel() or o_lo.stride() == o.stride():
+        return o_lo
+    return torch.empty_strided(o.shape, o.stride(), device=o.device, dtype=o.dtype).copy_(o_lo)
+
+
+def _sp2norm_flash_bwd(q, k, v, o, do, row_sums, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True,
+                       o_lo=None):
+    """Run the fused backward; return (dq, dk, dv) like kernels.py:1934-1989.
+
+    o_lo (optional): the forward's residual (``with_residual=True``)."""
     if _tracing(q, k, v, o, do, row_sums):
-        return _ops().flash_bwd(q, k, v, o, do, row_sums, float(scale), int(window_size), bool(use_fast_sqrt))
-    return _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt)
+        lo = o_lo if o_lo is not None else o.new_empty(0)
+        return _ops().flash_bwd(q, k, v, o, lo, do, row_sums, float(scale), int(window_size), bool(use_fast_sqrt))
+    return _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt, o_lo=o_lo)
 
 
-def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt):
+def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt, o_lo=None):
     B, H_q, T, D = q.shape
     H_kv = k.shape[1]
     do = _flash_ready(do)
+    o_lo = _match_strides(o_lo, o)
     dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     dk = torch.empty(k.shape, device=q.device, dtype=q.dtype)
     dv = torch.empty(v.shape, device=q.device, dtype=q.dtype)
@@ -550,7 +575,7 @@ def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqr
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
     with _on(q.device):
         st = lib.sa_flash_bwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), row_sums.data_ptr(),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), _ptr(o_lo), do.data_ptr(), row_sums.data_ptr(),
             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
             B, H_q, H_kv, T, D,
             _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o), _lib.strides(do),
@@ -566,8 +591,10 @@ class _SP2NormFlashAttentionFn(torch.autograd.Function):
     def forward(ctx, q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt):
         if not _tracing(q, k, v):  # the traced op readies its inputs itself
             q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
-        o, row_sums = _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt)
-        ctx.save_for_backward(q, k, v, o, row_sums)
+        train = any(ctx.needs_input_grad[:3])
+        res = _sp2norm_flash_fwd(q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt, with_residual=train)
+        o, row_sums = res[0], res[1]
+        ctx.save_for_backward(q, k, v, o, row_sums, res[2] if train else None)
         ctx.scale = scale
         ctx.n_kv_groups = n_kv_groups
         ctx.window_size = window_size
@@ -576,9 +603,9 @@ class _SP2NormFlashAttentionFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output):
-        q, k, v, o, row_sums = ctx.saved_tensors
+        q, k, v, o, row_sums, o_lo = ctx.saved_tensors
         dq, dk, dv = _sp2norm_flash_bwd(q, k, v, o, grad_output, row_sums, ctx.scale, ctx.n_kv_groups,
-                                        ctx.window_size, use_fast_sqrt=ctx.use_fast_sqrt)
+                                        ctx.window_size, use_fast_sqrt=ctx.use_fast_sqrt, o_lo=o_lo)
         return dq, dk, dv, None, None, None, None
 
 
@@ -600,7 +627,8 @@ def sp2norm_flash_attention(q, k, v, *, scale=None, window_size=0, exact_math=Fa
     return _SP2NormFlashAttentionFn.apply(q, k, v, scale, H_q // H_kv, window_size, not exact_math)
 
 
-def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=0, exact_math=False):
+def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=0, exact_math=False,
+                                  return_residual=False):
     """Forward of a block of queries against a key prefix (``sa_flash_fwd_chunk``).
 
     q: [B, H_q, Tq, D] at global positions q_offset .. q_offset+Tq-1;
@@ -609,7 +637,9 @@ def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=
     sequence into query chunks that each see their key prefix reproduces the
     whole forward.  The building block of context parallelism
     (``smooth_attn.parallel.context_parallel_attention``).  Returns
-    (o [B, H_q, Tq, D], row_sums [B, H_q, Tq]).
+    (o [B, H_q, Tq, D], row_sums [B, H_q, Tq]), plus o_lo (the residual of
+    o's rounding, for ``sp2norm_flash_attention_chunk_bwd``) when
+    ``return_residual``.
     """
     assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
     B, H_q, Tq, D = q.shape
@@ -620,49 +650,55 @@ def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if _tracing(q, k, v):
-        return _ops().flash_fwd_chunk(q, k, v, int(q_offset), float(scale), int(window_size), bool(exact_math))
-    return _flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math)
+        o, rs, o_lo = _ops().flash_fwd_chunk(q, k, v, int(q_offset), float(scale), int(window_size),
+                                             bool(exact_math), bool(return_residual))
+        return (o, rs, o_lo) if return_residual else (o, rs)
+    return _flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math, return_residual)
 
 
-def _flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math):
+def _flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math, with_residual=False):
     B, H_q, Tq, D = q.shape
     H_kv, Tk = k.shape[1], k.shape[2]
     q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
     o = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    o_lo = torch.empty(q.shape, device=q.device, dtype=q.dtype) if with_residual else None
     row_sums = torch.empty(B, H_q, Tq, device=q.device, dtype=torch.float32)
     if q.numel() == 0:
-        return o, row_sums
+        return (o, row_sums, o_lo) if with_residual else (o, row_sums)
     with _on(q.device):
         st = _lib.load().sa_flash_fwd_chunk(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), row_sums.data_ptr(),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), _ptr(o_lo), row_sums.data_ptr(),
             B, H_q, H_kv, Tq, Tk, int(q_offset), D, _lib.strides(q), _lib.strides(k), _lib.strides(v),
             _lib.strides(o), float(scale), int(window_size), int(bool(exact_math)), _DTYPE_CODE[q.dtype], _stream(q),
         )
     _lib.check(st, "sa_flash_fwd_chunk")
-    return o, row_sums
+    return (o, row_sums, o_lo) if with_residual else (o, row_sums)
 
 
 def sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, row_sums, q_offset, *, scale=None, window_size=0,
-                                      exact_math=False):
+                                      exact_math=False, o_lo=None):
     """Backward of ``sp2norm_flash_attention_chunk`` (``sa_flash_bwd_chunk``).
 
     Returns (dq [B, H_q, Tq, D], dk, dv [B, H_kv, Tk, D]): dq is complete for
     the query block; dk / dv hold this block's contribution only (the
     context-parallel backward sums them over every rank's query blocks).
+    o_lo (optional): the chunk forward's residual (``return_residual=True``).
     """
     D = q.shape[3]
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if _tracing(q, k, v, o, do, row_sums):
-        return _ops().flash_bwd_chunk(q, k, v, o, do, row_sums, int(q_offset), float(scale), int(window_size),
+        lo = o_lo if o_lo is not None else o.new_empty(0)
+        return _ops().flash_bwd_chunk(q, k, v, o, lo, do, row_sums, int(q_offset), float(scale), int(window_size),
                                       bool(exact_math))
-    return _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math)
+    return _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math, o_lo)
 
 
-def _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math):
+def _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math, o_lo=None):
     B, H_q, Tq, D = q.shape
     H_kv, Tk = k.shape[1], k.shape[2]
     q, k, v, o, do = (_flash_ready(t) for t in (q, k, v, o, do))
+    o_lo = _match_strides(o_lo, o)
     dq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
     dk = torch.empty(k.shape, device=q.device, dtype=q.dtype)
     dv = torch.empty(v.shape, device=q.device, dtype=q.dtype)
@@ -673,7 +709,7 @@ def _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_si
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
     with _on(q.device):
         st = lib.sa_flash_bwd_chunk(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), row_sums.data_ptr(),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), _ptr(o_lo), do.data_ptr(), row_sums.data_ptr(),
             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
             B, H_q, H_kv, Tq, Tk, int(q_offset), D,
             _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o), _lib.strides(do),

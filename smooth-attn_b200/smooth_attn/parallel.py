@@ -145,6 +145,16 @@ def _reduce_scatter_zigzag(full: torch.Tensor, group=None, dim: int = 2) -> torc
     return total[rank].clone()
 
 
+def _key_span(c, C, window_size):
+    """Keys [s0, e) that the queries of chunk c (positions c*C .. c*C+C-1) can
+    see: the causal prefix, cut on the left by a sliding window.  The chunk
+    kernels take keys from position 0, so callers pass the slice and the query
+    offset c*C - s0 (relative positions keep the causal / window rule)."""
+    e = (c + 1) * C
+    s0 = max(0, c * C - window_size + 1) if window_size > 0 else 0
+    return s0, e
+
+
 def _cp_gather_kv(k, v, group):
     kv = torch.stack([k, v]).contiguous()
     return zigzag_merge(_all_gather(kv, group), dim=3)  # [2, B, Hkv, T, D] in sequence order
@@ -164,15 +174,19 @@ class _ContextParallelAttnFn(torch.autograd.Function):
         rank = dist.get_rank(group)
         C = q.shape[2] // 2
         full = _cp_gather_kv(k, v, group)
-        outs, sums = [], []
+        train = any(ctx.needs_input_grad[:3])
+        outs, sums, los = [], [], []
         for i, c in enumerate(zigzag_chunk_ids(world, rank)):
             qc = q[:, :, i * C:(i + 1) * C]
-            o, r = kernels.sp2norm_flash_attention_chunk(qc, full[0, :, :, :(c + 1) * C], full[1, :, :, :(c + 1) * C],
-                                                         c * C, scale=scale, window_size=window_size)
-            outs.append(o)
-            sums.append(r)
+            s0, e = _key_span(c, C, window_size)
+            res = kernels.sp2norm_flash_attention_chunk(qc, full[0, :, :, s0:e], full[1, :, :, s0:e], c * C - s0,
+                                                        scale=scale, window_size=window_size, return_residual=train)
+            outs.append(res[0])
+            sums.append(res[1])
+            if train:
+                los.append(res[2])
         o = torch.cat(outs, dim=2)
-        ctx.save_for_backward(q, k, v, o, torch.cat(sums, dim=2))
+        ctx.save_for_backward(q, k, v, o, torch.cat(sums, dim=2), torch.cat(los, dim=2) if train else None)
         ctx.group, ctx.scale, ctx.window_size = group, scale, window_size
         return o
 
@@ -180,7 +194,7 @@ class _ContextParallelAttnFn(torch.autograd.Function):
     def backward(ctx, do):
         from . import kernels
 
-        q, k, v, o, sums = ctx.saved_tensors
+        q, k, v, o, sums, o_lo = ctx.saved_tensors
         group = ctx.group
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
@@ -192,13 +206,14 @@ class _ContextParallelAttnFn(torch.autograd.Function):
         dqs = []
         for i, c in enumerate(zigzag_chunk_ids(world, rank)):
             sl = slice(i * C, (i + 1) * C)
-            e = (c + 1) * C
+            s0, e = _key_span(c, C, ctx.window_size)
             dq, dk, dv = kernels.sp2norm_flash_attention_chunk_bwd(
-                q[:, :, sl], full[0, :, :, :e], full[1, :, :, :e], o[:, :, sl], do[:, :, sl].contiguous(),
-                sums[:, :, sl].contiguous(), c * C, scale=ctx.scale, window_size=ctx.window_size)
+                q[:, :, sl], full[0, :, :, s0:e], full[1, :, :, s0:e], o[:, :, sl], do[:, :, sl].contiguous(),
+                sums[:, :, sl].contiguous(), c * C - s0, scale=ctx.scale, window_size=ctx.window_size,
+                o_lo=None if o_lo is None else o_lo[:, :, sl])
             dqs.append(dq)
-            dk_full[:, :, :e] += dk.float()
-            dv_full[:, :, :e] += dv.float()
+            dk_full[:, :, s0:e] += dk.float()
+            dv_full[:, :, s0:e] += dv.float()
         assert dk_full.shape[2] == T
         dk_loc = _reduce_scatter_zigzag(dk_full, group).to(k.dtype)
         dv_loc = _reduce_scatter_zigzag(dv_full, group).to(v.dtype)

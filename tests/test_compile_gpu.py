@@ -77,7 +77,7 @@ def test_compiled_forward_only_paths_match_eager():
 
 def test_opcheck_all_ops():
     q, k, v = (randn((1, h, 130, 64), h, torch.bfloat16, CUDA) for h in (4, 2, 2))
-    o, rs = OPS.flash_fwd(q, k, v, 0.125, 0, True)
+    o, rs, lo = OPS.flash_fwd(q, k, v, 0.125, 0, True, True)
     do = randn(q.shape, 9, torch.bfloat16, CUDA)
     x = randn((2, 96, 96), 3, torch.float32, CUDA)
     y, xr = OPS.norm_fwd(x, 2.0, 0.5, 2, True, True)
@@ -90,10 +90,13 @@ def test_opcheck_all_ops():
         (OPS.norm_fwd, (x, 2.0, 0.5, 2, True, True)),
         (OPS.norm_fwd, (x.view(-1, 96), 2.0, 0.5, 3, False, False)),
         (OPS.norm_causal_bwd, (x, randn(x.shape, 8, torch.float32, CUDA), xr, 2.0, 0.5, 2)),
-        (OPS.flash_fwd, (q, k, v, 0.125, 0, True)),
-        (OPS.flash_bwd, (q, k, v, o, do, rs, 0.125, 0, True)),
-        (OPS.flash_fwd_chunk, (q[:, :, 64:], k, v, 64, 0.125, 0, False)),
-        (OPS.flash_bwd_chunk, (q[:, :, 64:].contiguous(), k, v, o[:, :, 64:].contiguous(), do[:, :, 64:].contiguous(),
+        (OPS.flash_fwd, (q, k, v, 0.125, 0, True, True)),
+        (OPS.flash_fwd, (q, k, v, 0.125, 0, True, False)),
+        (OPS.flash_bwd, (q, k, v, o, lo, do, rs, 0.125, 0, True)),
+        (OPS.flash_bwd, (q, k, v, o, o.new_empty(0), do, rs, 0.125, 0, True)),
+        (OPS.flash_fwd_chunk, (q[:, :, 64:], k, v, 64, 0.125, 0, False, True)),
+        (OPS.flash_bwd_chunk, (q[:, :, 64:].contiguous(), k, v, o[:, :, 64:].contiguous(),
+                               lo[:, :, 64:].contiguous(), do[:, :, 64:].contiguous(),
                                rs[:, :, 64:].contiguous(), 64, 0.125, 0, False)),
         (OPS.rope_flash_fwd, (q, k, v, cos, sin, 0.125, 0)),
         (OPS.fp8_flash_fwd, (q, k, v, 0.125, 0)),

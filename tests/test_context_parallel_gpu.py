@@ -16,7 +16,7 @@ from tests._util import assert_close, np32, randn
 
 pytestmark = pytest.mark.gpu
 CUDA = "cuda"
-FWD_TOL = dict(rtol=5e-2, atol=2e-2)  # bf16 attention output vs the fp32 oracle (as the flash tests)
+FWD_TOL = dict(rtol=2e-2, atol=1e-2)  # bf16 attention output vs the fp32 oracle (as the flash tests)
 
 
 @pytest.fixture(autouse=True)
@@ -51,7 +51,7 @@ def test_chunks_reproduce_full_forward(T, chunks, window):
     assert (got.float() - full.float()).abs().max().item() <= 2e-2
 
 
-BWD_TOL = dict(rtol=0.1, atol=5e-2)  # the flash tests' backward tolerance
+BWD_TOL = dict(rtol=2e-2, atol=1e-2)  # the flash tests' backward tolerance
 
 
 @pytest.mark.parametrize("Tq,Tk,off,D,window,Hq,Hkv", [(128, 256, 128, 128, 0, 4, 2), (100, 300, 200, 64, 0, 2, 2),
@@ -65,8 +65,8 @@ def test_chunk_backward_matches_oracle(Tq, Tk, off, D, window, Hq, Hkv):
     k = randn((1, Hkv, Tk, D), Tk, torch.bfloat16, CUDA)
     v = randn((1, Hkv, Tk, D), Tk + 1, torch.bfloat16, CUDA)
     do = randn((1, Hq, Tq, D), 7, torch.bfloat16, CUDA)
-    o, rs = sa.sp2norm_flash_attention_chunk(q, k, v, off, window_size=window)
-    dq, dk, dv = sa.kernels.sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, rs, off, window_size=window)
+    o, rs, lo = sa.sp2norm_flash_attention_chunk(q, k, v, off, window_size=window, return_residual=True)
+    dq, dk, dv = sa.kernels.sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, rs, off, window_size=window, o_lo=lo)
     rq, rk, rv = O.chunk_flash_attention_bwd(np32(q), np32(k), np32(v), np32(do), off, window_size=window)
     assert_close(np32(dq), rq, **BWD_TOL)
     assert_close(np32(dk), rk, **BWD_TOL)
@@ -77,11 +77,12 @@ def test_chunk_backward_matches_oracle(Tq, Tk, off, D, window, Hq, Hkv):
 
 
 def test_chunked_backward_reproduces_full_backward():
+    """Chunk backwards summed over a split sequence equal the full backward's
+    oracle gradients (dK / dV summed in fp32 over the chunks)."""
     T, chunks = 2048, 4
     q, k, v = (randn((1, h, T, 128), T + h, torch.bfloat16, CUDA) for h in (8, 2, 2))
     do = randn((1, 8, T, 128), 3, torch.bfloat16, CUDA)
-    qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
-    (sa.sp2norm_flash_attention(qr, kr, vr) * do).sum().backward()
+    rq, rk, rv = O.sp2norm_flash_attention_bwd(np32(q), np32(k), np32(v), np32(do))
     C = T // chunks
     dk_acc = torch.zeros(k.shape, dtype=torch.float32, device=CUDA)
     dv_acc = torch.zeros_like(dk_acc)
@@ -89,14 +90,15 @@ def test_chunked_backward_reproduces_full_backward():
     for c in range(chunks):
         e = (c + 1) * C
         qc, doc = q[:, :, c * C:e].contiguous(), do[:, :, c * C:e].contiguous()
-        o, rs = sa.sp2norm_flash_attention_chunk(qc, k[:, :, :e], v[:, :, :e], c * C)
-        dq, dk, dv = sa.kernels.sp2norm_flash_attention_chunk_bwd(qc, k[:, :, :e], v[:, :, :e], o, doc, rs, c * C)
+        o, rs, lo = sa.sp2norm_flash_attention_chunk(qc, k[:, :, :e], v[:, :, :e], c * C, return_residual=True)
+        dq, dk, dv = sa.kernels.sp2norm_flash_attention_chunk_bwd(qc, k[:, :, :e], v[:, :, :e], o, doc, rs, c * C,
+                                                                  o_lo=lo)
         dqs.append(dq)
         dk_acc[:, :, :e] += dk.float()
         dv_acc[:, :, :e] += dv.float()
-    assert_close(np32(torch.cat(dqs, dim=2)), np32(qr.grad), rtol=2e-2, atol=2e-2)
-    assert_close(np32(dk_acc), np32(kr.grad), rtol=5e-2, atol=5e-2)
-    assert_close(np32(dv_acc), np32(vr.grad), rtol=5e-2, atol=5e-2)
+    assert_close(np32(torch.cat(dqs, dim=2)), rq, **BWD_TOL)
+    assert_close(np32(dk_acc), rk, **BWD_TOL)
+    assert_close(np32(dv_acc), rv, **BWD_TOL)
 
 
 def _free_port():

@@ -18,11 +18,15 @@ pytestmark = pytest.mark.gpu
 CUDA = "cuda"
 G = np.load(Path(__file__).parent / "golden" / "golden.npz")
 
-# bf16 attention output vs the fp32 oracle on the same (bf16-rounded) inputs.
-# The kernel rounds the unnormalized y to bf16 before P.V exactly like the
-# reference (kernels.py:1621), so the reference's own flash tolerance applies.
-FWD_TOL = dict(rtol=5e-2, atol=2e-2)
-BWD_TOL = dict(rtol=0.1, atol=5e-2)
+# bf16 outputs and gradients vs the fp32 oracle on the same (bf16-rounded)
+# inputs, at the north-star tolerance: 2e-2 relative / 1e-2 absolute.  The
+# kernel rounds the unnormalized y to bf16 before P.V like the reference
+# (kernels.py:1621) and dS / P to bf16 before their MMAs; the backward forms
+# delta = rowsum(dO * o) from the forward's fp32 output (o + o_lo), which
+# keeps dQ / dK inside this bound (with the rounded o alone they reach
+# ~1.3x of it).
+FWD_TOL = dict(rtol=2e-2, atol=1e-2)
+BWD_TOL = dict(rtol=2e-2, atol=1e-2)
 
 
 @pytest.fixture(autouse=True)
@@ -58,7 +62,7 @@ def test_flash_attention_matches_eager_reference_case(T):
     q, k, v = _qkv(2, 4, 4, T, 32, seed=T)
     out_flash = sa.sp2norm_flash_attention(q, k, v)
     out_eager = sa.sp2norm_flash_attention_eager(q, k, v)
-    torch.testing.assert_close(out_flash.float(), out_eager.float(), atol=2e-2, rtol=5e-2)
+    torch.testing.assert_close(out_flash.float(), out_eager.float(), atol=1e-2, rtol=2e-2)
 
 
 def test_flash_rowsum_saved():
@@ -184,7 +188,7 @@ def test_flash_backward_reference_case():
     attn = sa.softplus_norm_causal_eager(torch.matmul(qr, kr.transpose(-2, -1)) * scale)
     (torch.matmul(attn, vr) * upstream).sum().backward()
     for got, ref in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
-        torch.testing.assert_close(got.float(), ref.float(), atol=5e-2, rtol=0.1)
+        torch.testing.assert_close(got.float(), ref.float(), atol=1e-2, rtol=2e-2)
 
 
 def test_flash_bwd_exact_math():
@@ -240,3 +244,39 @@ def test_zzz_flash_bwd_no_device_timeouts():
     from smooth_attn import _lib
 
     assert _lib.load().sa_device_status(1) == _lib.SA_OK
+
+
+# ---- residual output and large grids -------------------------------------------
+
+
+def test_flash_residual_is_rounding_of_fp32_output():
+    """o_lo carries the part of the fp32 output that the bf16 o rounded away:
+    |o_lo| <= half an ulp of o, and o + o_lo is closer to the oracle than o."""
+    from smooth_attn.kernels import _sp2norm_flash_fwd
+
+    q, k, v = _qkv(1, 4, 2, 300, 128, seed=17)
+    o, rs, lo = _sp2norm_flash_fwd(q, k, v, 1.0 / 128 ** 0.5, with_residual=True)
+    o0, _ = _sp2norm_flash_fwd(q, k, v, 1.0 / 128 ** 0.5)
+    assert torch.equal(o, o0)  # the residual does not change o
+    of, lf = o.float(), lo.float()
+    assert (lf.abs() <= of.abs() * 2.0 ** -8 + 1e-30).all()
+    ref, _ = _fwd_ref(q, k, v)
+    err_hi = np.abs(np32(o) - ref).mean()
+    err_hl = np.abs(np32(of + lf) - ref).mean()
+    assert err_hl < err_hi
+
+
+def test_flash_more_than_65535_heads():
+    """B * H above the old 65535 grid limit: fwd and bwd run and sampled heads match."""
+    B, H, T, D = 2, 33000, 5, 32
+    q, k, v = (t.requires_grad_(True) for t in _qkv(B, H, H, T, D, seed=65))
+    do = randn((B, H, T, D), 66, torch.bfloat16, CUDA)
+    o = sa.sp2norm_flash_attention(q, k, v)
+    o.backward(do)
+    for b, h in ((0, 0), (1, 32999), (1, 16500)):
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        ref = O.sp2norm_flash_attention(np32(q[sl]), np32(k[sl]), np32(v[sl]))
+        assert_close(np32(o[sl]), ref, **FWD_TOL)
+        dq, dk, dv = O.sp2norm_flash_attention_bwd(np32(q[sl]), np32(k[sl]), np32(v[sl]), np32(do[sl]))
+        for got, r in ((q.grad[sl], dq), (k.grad[sl], dk), (v.grad[sl], dv)):
+            assert_close(np32(got), r, **BWD_TOL)

@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 CUDA = "cuda"
 G = np.load(Path(__file__).parent / "golden" / "golden.npz")
 # same quantized operands: only accumulation order and bf16 output rounding differ
-FP8_TOL = dict(rtol=5e-2, atol=2e-2)
+FP8_TOL = dict(rtol=2e-2, atol=1e-2)  # kernel vs the oracle on the same E4M3 inputs
 
 
 @pytest.fixture(autouse=True)
@@ -97,7 +97,7 @@ def test_fp8_scale_and_large_values():
     q2, v2 = q * 100, v * 100
     o2 = sa.sp2norm_fp8_flash_attention(q2, k, v2, scale=0.0002)
     ref2 = O.fp8_flash_attention(np32(q2), np32(k), np32(v2), scale=0.0002)
-    assert_close(np32(o2), ref2, rtol=5e-2, atol=2.0)  # outputs ~100x larger
+    assert_close(np32(o2), ref2, rtol=2e-2, atol=1.0)  # outputs ~100x larger: 1e-2 x 100
 
 
 def test_fp8_rejects_bad_arguments():

@@ -83,7 +83,7 @@ def test_causal_golden(name):
     if dtype == torch.float32:
         assert_close(np32(x.grad), ref, rtol=1e-5, atol=1e-6 * max(1.0, np.abs(ref).max()))
     else:
-        assert_close(np32(x.grad), ref, rtol=2e-2, atol=1e-2 * max(1.0, np.abs(ref).max()))
+        assert_close(np32(x.grad), ref, rtol=2e-2, atol=1e-2)
 
 
 @pytest.mark.parametrize("name", sorted({k.split("/")[0] for k in G.files if k.startswith("r_")}))
@@ -153,7 +153,7 @@ def _bwd_check(x, g, fam, dtype):
     if dtype == torch.float32:
         assert_close(np32(xr.grad), ref, rtol=1e-5, atol=1e-6 * scale)
     else:
-        assert_close(np32(xr.grad), ref, rtol=2e-2, atol=1e-2 * scale)
+        assert_close(np32(xr.grad), ref, rtol=2e-2, atol=1e-2)
     assert xr.grad.dtype == x.dtype
     L = x.shape[-1]
     assert np.all(np32(xr.grad)[..., ~O.causal_mask(L)] == 0.0)
@@ -225,7 +225,7 @@ def test_baseline_config3_bwd_slice_and_linearity():
     y.backward(g)
     for b, h in ((0, 0), (3, 31)):
         ref = O.softplus_norm_causal_bwd(np32(x[b, h]), np32(g[b, h]))
-        assert_close(np32(x.grad[b, h]), ref, rtol=2e-2, atol=1e-2 * max(1.0, float(np.abs(ref).max())))
+        assert_close(np32(x.grad[b, h]), ref, rtol=2e-2, atol=1e-2)
     gx = x.grad.clone()
     x.grad = None
     y = sa.softplus_norm_causal(x)

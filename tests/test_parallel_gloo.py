@@ -115,12 +115,14 @@ def _worker(rank, world, port, mode, q):
             # the oracle (CPU ranks, no GPU)
             import smooth_attn.kernels as K
 
-            def chunk(qc, kp, vp, off, scale=None, window_size=0):
+            def chunk(qc, kp, vp, off, scale=None, window_size=0, return_residual=False):
                 o = O.chunk_flash_attention(qc.numpy(), kp.numpy(), vp.numpy(), off, scale=scale,
                                             window_size=window_size)
-                return torch.from_numpy(o), torch.ones(qc.shape[:3])
+                o = torch.from_numpy(o)
+                res = (o, torch.ones(qc.shape[:3]))
+                return res + (torch.zeros_like(o),) if return_residual else res
 
-            def chunk_bwd(qc, kp, vp, o, do, sums, off, scale=None, window_size=0):
+            def chunk_bwd(qc, kp, vp, o, do, sums, off, scale=None, window_size=0, o_lo=None):
                 g = O.chunk_flash_attention_bwd(qc.detach().numpy(), kp.detach().numpy(), vp.detach().numpy(),
                                                 do.numpy(), off, scale=scale, window_size=window_size)
                 return tuple(torch.from_numpy(t) for t in g)
@@ -187,7 +189,7 @@ def test_gloo_world2_rank_failure_surfaces_as_error():
     assert res[0][1] == "error"  # the survivor's collective errors out instead of hanging
 
 
-@pytest.mark.parametrize("mode", ["cp", "cp7"])
+@pytest.mark.parametrize("mode", ["cp", "cp7", "cp13"])
 def test_gloo_world2_context_parallel_equals_single_process(mode):
     res = _run(mode)
     assert [r[1] for r in res] == ["ok", "ok"], res
