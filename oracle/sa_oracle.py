@@ -226,81 +226,42 @@ def sp2norm_flash_attention(q, k, v, scale=None, window_size=0, acc=np.float32, 
     return o
 
 
-def sp2norm_flash_attention_bwd(q, k, v, do, scale=None, window_size=0, acc=np.float32):
-    """Gradients (dq, dk, dv) of ``sum(sp2norm_flash_attention(q,k,v) * do)``.
+def _flash_bwd_core(q, k_in, v_in, do, mask, scale, acc, emulate):
+    """Closed-form flash backward over a boolean visibility mask [Tq, Tk].
 
-    Closed form of the reference's fused backward (kernels.py:1723-1909):
-      delta = rowsum(dO * O); dP = dO V^T; dY = (dP - delta)/R;
-      dS = dY * 4 sp sp' * scale;  dQ = dS K;  dK = dS^T Q;  dV = (y/R)^T dO
-    GQA gradients of K/V are summed over the query heads of each group.
-    """
-    q = _as_f(q, acc)
-    k_in = _as_f(k, acc)
-    v_in = _as_f(v, acc)
-    do = _as_f(do, acc)
-    B, Hq, T, D = q.shape
-    Hkv = k_in.shape[1]
-    k = _expand_kv(k_in, Hq)
-    v = _expand_kv(v_in, Hq)
-    if scale is None:
-        scale = 1.0 / math.sqrt(D)
-    s = np.matmul(q, np.swapaxes(k, -1, -2)) * acc(scale)
-    a = acc(2.0) * s - acc(1.0)
-    rt = np.sqrt(a * a + acc(4.0))
-    sp = acc(0.5) * (a + rt)
-    spp = acc(0.5) * (acc(1.0) + a / rt)
-    mask = _flash_mask(T, window_size)
-    y = np.where(mask, sp * sp, acc(0.0))
-    r = y.sum(axis=-1, keepdims=True) + acc(EPS)
-    p = y / r
-    o = np.matmul(p, v)
-    delta = (do * o).sum(axis=-1, keepdims=True)
-    dp = np.matmul(do, np.swapaxes(v, -1, -2))
-    dy = np.where(mask, (dp - delta) / r, acc(0.0))
-    ds = dy * acc(4.0) * sp * spp * acc(scale)
-    dq = np.matmul(ds, k)
-    dk = np.matmul(np.swapaxes(ds, -1, -2), q)
-    dv = np.matmul(np.swapaxes(p, -1, -2), do)
-    if Hkv != Hq:
-        g = Hq // Hkv
-        dk = dk.reshape(B, Hkv, g, T, D).sum(axis=2)
-        dv = dv.reshape(B, Hkv, g, T, D).sum(axis=2)
-    return dq, dk, dv
-
-
-def chunk_flash_attention_bwd(q, k, v, do, q_offset, scale=None, window_size=0, acc=np.float32):
-    """Gradients of ``sum(chunk_flash_attention(q, k, v, q_offset) * do)``:
-    dq for the query block, dk / dv for keys 0 .. Tk-1 (this block's
-    contribution).  Same closed form as sp2norm_flash_attention_bwd with the
-    mask in global positions."""
-    q = _as_f(q, acc)
-    k_in = _as_f(k, acc)
-    v_in = _as_f(v, acc)
-    do = _as_f(do, acc)
+    emulate=False: the reference's exact algebra in ``acc`` (kernels.py:1723-1909).
+    emulate=True: the same algebra with the 16-bit rounding points of the
+    B200 kernels (test infrastructure for telling operand rounding apart from
+    defects): the forward's normalizer and output use y rounded to bf16
+    (P.V multiplies bf16 y, as the reference does at kernels.py:1621, and the
+    normalizer sums those same rounded y), dS is rounded to bf16 before the dQ
+    / dK products and P = y / R before the dV product (the reference's
+    rounding points, kernels.py:1776, 1894)."""
     B, Hq, Tq, D = q.shape
     Hkv, Tk = k_in.shape[1], k_in.shape[2]
     k = _expand_kv(k_in, Hq)
     v = _expand_kv(v_in, Hq)
-    if scale is None:
-        scale = 1.0 / math.sqrt(D)
-    qp = np.arange(Tq)[:, None] + q_offset
-    kp = np.arange(Tk)[None, :]
-    mask = kp <= qp
-    if window_size > 0:
-        mask &= (qp - kp) < window_size
     s = np.matmul(q, np.swapaxes(k, -1, -2)) * acc(scale)
     a = acc(2.0) * s - acc(1.0)
     rt = np.sqrt(a * a + acc(4.0))
     sp = acc(0.5) * (a + rt)
     spp = acc(0.5) * (acc(1.0) + a / rt)
     y = np.where(mask, sp * sp, acc(0.0))
-    r = y.sum(axis=-1, keepdims=True) + acc(EPS)
+    if emulate:
+        yh = round_bf16(y).astype(acc)
+        r = yh.sum(axis=-1, keepdims=True) + acc(EPS)
+        o = np.matmul(yh / r, v)
+    else:
+        r = y.sum(axis=-1, keepdims=True) + acc(EPS)
+        o = np.matmul(y / r, v)
     p = y / r
-    o = np.matmul(p, v)
     delta = (do * o).sum(axis=-1, keepdims=True)
     dp = np.matmul(do, np.swapaxes(v, -1, -2))
     dy = np.where(mask, (dp - delta) / r, acc(0.0))
     ds = dy * acc(4.0) * sp * spp * acc(scale)
+    if emulate:
+        ds = round_bf16(ds).astype(acc)
+        p = round_bf16(p).astype(acc)
     dq = np.matmul(ds, k)
     dk = np.matmul(np.swapaxes(ds, -1, -2), q)
     dv = np.matmul(np.swapaxes(p, -1, -2), do)
@@ -309,6 +270,41 @@ def chunk_flash_attention_bwd(q, k, v, do, q_offset, scale=None, window_size=0, 
         dk = dk.reshape(B, Hkv, g, Tk, D).sum(axis=2)
         dv = dv.reshape(B, Hkv, g, Tk, D).sum(axis=2)
     return dq, dk, dv
+
+
+def sp2norm_flash_attention_bwd(q, k, v, do, scale=None, window_size=0, acc=np.float32, emulate=False):
+    """Gradients (dq, dk, dv) of ``sum(sp2norm_flash_attention(q,k,v) * do)``.
+
+    Closed form of the reference's fused backward (kernels.py:1723-1909):
+      delta = rowsum(dO * O); dP = dO V^T; dY = (dP - delta)/R;
+      dS = dY * 4 sp sp' * scale;  dQ = dS K;  dK = dS^T Q;  dV = (y/R)^T dO
+    GQA gradients of K/V are summed over the query heads of each group.
+    ``emulate=True`` applies the 16-bit rounding points (see _flash_bwd_core).
+    """
+    q = _as_f(q, acc)
+    T, D = q.shape[-2], q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    return _flash_bwd_core(q, _as_f(k, acc), _as_f(v, acc), _as_f(do, acc), _flash_mask(T, window_size), scale,
+                           acc, emulate)
+
+
+def chunk_flash_attention_bwd(q, k, v, do, q_offset, scale=None, window_size=0, acc=np.float32, emulate=False):
+    """Gradients of ``sum(chunk_flash_attention(q, k, v, q_offset) * do)``:
+    dq for the query block, dk / dv for keys 0 .. Tk-1 (this block's
+    contribution).  Same closed form as sp2norm_flash_attention_bwd with the
+    mask in global positions."""
+    q = _as_f(q, acc)
+    Tq, D = q.shape[-2], q.shape[-1]
+    Tk = np.shape(k)[-2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    qp = np.arange(Tq)[:, None] + q_offset
+    kp = np.arange(Tk)[None, :]
+    mask = kp <= qp
+    if window_size > 0:
+        mask &= (qp - kp) < window_size
+    return _flash_bwd_core(q, _as_f(k, acc), _as_f(v, acc), _as_f(do, acc), mask, scale, acc, emulate)
 
 
 def paged_decode_attention(q, k_cache, v_cache, block_table, context_lens, scale=None, acc=np.float32):

@@ -152,8 +152,16 @@ __device__ __forceinline__ float squareplus_regs(const uint32_t (&r)[32], uint32
       y.x = ok0 ? y.x : 0.f;
       y.y = ok1 ? y.y : 0.f;
     }
-    sum = fadd2(sum, y);
     pk[e / 2] = BF16 ? pack2_bf16(y.x, y.y) : pack2_f16(y.x, y.y);
+    // the normalizer sums the 16-bit y that P.V multiplies, so every output
+    // row is a convex combination of V rows (sum of weights exactly 1)
+    float2 yr;
+    if (BF16) {
+      yr = make_float2(__uint_as_float(pk[e / 2] << 16), __uint_as_float(pk[e / 2] & 0xffff0000u));
+    } else {
+      yr = __half22float2(*reinterpret_cast<const __half2*>(&pk[e / 2]));
+    }
+    sum = fadd2(sum, yr);
   }
   tmem_st16(taddr_p, pk);
   return sum.x + sum.y;

@@ -7,12 +7,13 @@ backward on zig-zag sequence blocks against the single-GPU autograd."""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 
 import smooth_attn as sa
 from oracle import sa_oracle as O
-from tests._util import assert_close, np32, randn
+from tests._util import assert_close, check_bf16_grads, np32, randn
 
 pytestmark = pytest.mark.gpu
 CUDA = "cuda"
@@ -67,10 +68,11 @@ def test_chunk_backward_matches_oracle(Tq, Tk, off, D, window, Hq, Hkv):
     do = randn((1, Hq, Tq, D), 7, torch.bfloat16, CUDA)
     o, rs, lo = sa.sp2norm_flash_attention_chunk(q, k, v, off, window_size=window, return_residual=True)
     dq, dk, dv = sa.kernels.sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, rs, off, window_size=window, o_lo=lo)
-    rq, rk, rv = O.chunk_flash_attention_bwd(np32(q), np32(k), np32(v), np32(do), off, window_size=window)
-    assert_close(np32(dq), rq, **BWD_TOL)
-    assert_close(np32(dk), rk, **BWD_TOL)
-    assert_close(np32(dv), rv, **BWD_TOL)
+    args = (np32(q), np32(k), np32(v), np32(do), off)
+    ref = O.chunk_flash_attention_bwd(*args, window_size=window, acc=np.float64)
+    emu = O.chunk_flash_attention_bwd(*args, window_size=window, emulate=True)
+    for g, r, m in zip((dq, dk, dv), ref, emu):
+        check_bf16_grads(np32(g), r, m, **BWD_TOL)
     if window:
         first_seen = max(0, off - window + 1)
         assert (dk[:, :, :first_seen] == 0).all() and (dv[:, :, :first_seen] == 0).all()
@@ -82,7 +84,9 @@ def test_chunked_backward_reproduces_full_backward():
     T, chunks = 2048, 4
     q, k, v = (randn((1, h, T, 128), T + h, torch.bfloat16, CUDA) for h in (8, 2, 2))
     do = randn((1, 8, T, 128), 3, torch.bfloat16, CUDA)
-    rq, rk, rv = O.sp2norm_flash_attention_bwd(np32(q), np32(k), np32(v), np32(do))
+    args = (np32(q), np32(k), np32(v), np32(do))
+    ref = O.sp2norm_flash_attention_bwd(*args, acc=np.float64)
+    emu = O.sp2norm_flash_attention_bwd(*args, emulate=True)
     C = T // chunks
     dk_acc = torch.zeros(k.shape, dtype=torch.float32, device=CUDA)
     dv_acc = torch.zeros_like(dk_acc)
@@ -96,9 +100,8 @@ def test_chunked_backward_reproduces_full_backward():
         dqs.append(dq)
         dk_acc[:, :, :e] += dk.float()
         dv_acc[:, :, :e] += dv.float()
-    assert_close(np32(torch.cat(dqs, dim=2)), rq, **BWD_TOL)
-    assert_close(np32(dk_acc), rk, **BWD_TOL)
-    assert_close(np32(dv_acc), rv, **BWD_TOL)
+    for g, r, m in zip((torch.cat(dqs, dim=2), dk_acc, dv_acc), ref, emu):
+        check_bf16_grads(np32(g), r, m, **BWD_TOL)
 
 
 def _free_port():

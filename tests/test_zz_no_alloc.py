@@ -18,6 +18,7 @@ The file is named to be collected last.
 
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
@@ -25,7 +26,7 @@ import smooth_attn as sa
 from oracle import sa_oracle as O
 from smooth_attn import _lib
 from smooth_attn.kernels import _sp2norm_flash_fwd
-from tests._util import assert_close, np32, randn
+from tests._util import check_bf16_grads, np32, randn
 
 pytestmark = pytest.mark.gpu
 
@@ -69,9 +70,11 @@ def test_noalloc_bwd_matches_allocating_entry_point_twice(Hq, Hkv, T, D):
         assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2])
         # dQ: same partials, fp32 atomics in another order, then one bf16 rounding
         torch.testing.assert_close(got[0].float(), ref[0].float(), rtol=1e-2, atol=1e-2)
-        oq, ok, ov = O.sp2norm_flash_attention_bwd(np32(q), np32(k), np32(v), np32(do), scale=scale)
-        for g, r in zip(got, (oq, ok, ov)):
-            assert_close(np32(g), r, rtol=2e-2, atol=1e-2)
+        args = (np32(q), np32(k), np32(v), np32(do))
+        ref64 = O.sp2norm_flash_attention_bwd(*args, scale=scale, acc=np.float64)
+        emu = O.sp2norm_flash_attention_bwd(*args, scale=scale, emulate=True)
+        for g, r, m in zip(got, ref64, emu):
+            check_bf16_grads(np32(g), r, m, rtol=2e-2, atol=1e-2)
 
 
 def test_noalloc_rejects_problem_larger_than_scratch():
