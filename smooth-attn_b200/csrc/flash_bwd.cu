@@ -502,7 +502,7 @@ __device__ __forceinline__ bool ew_all(bool v) {
 // -cd[m] = -delta*scale/R, so with t = a + sqrt(a^2+4) = 2 sp and
 // h = 1 + a rsqrt(a^2+4) = 2 sp':
 //   P  = sp^2 / R                      = t*t*c4
-//   dS = (dP - delta)/R * 4 sp sp' s   = (dP*cs - cd) * t*h
+//   dS = (dP - delta)/R * 4 sp sp' s   = (dP*cs - cd) * t*h = (dP*cs - cd) * t*t*rsqrt(a^2+4)
 // Both 32-column TMEM loads are issued together (one latency); results are
 // packed and stored 16 columns at a time to keep register use low.
 template <bool BF16, bool EXACT, bool MASK>
@@ -537,11 +537,13 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
         const float2 w = ffma2(a, a, make_float2(4.0f, 4.0f));
         const float2 rs = make_float2(rsqrt_approx(w.x), rsqrt_approx(w.y));
         const float2 t = EXACT ? make_float2(a.x + sqrtf(w.x), a.y + sqrtf(w.y)) : ffma2(w, rs, a);
-        const float2 hh = ffma2(a, rs, make_float2(1.0f, 1.0f));
-        float2 pp = fmul2(fmul2(t, t), c4p[u / 2]);
+        // 4 sp sp' = t (1 + a rsqrt(w)) = t^2 rsqrt(w): one multiply fewer, and
+        // no cancellation in 1 + a rsqrt(w) for very negative a
+        const float2 tt = fmul2(t, t);
+        float2 pp = fmul2(tt, c4p[u / 2]);
         float2 ds = fmul2(ffma2(make_float2(__uint_as_float(dv[idx]), __uint_as_float(dv[idx + 1])), csp[u / 2],
                                 cdp[u / 2]),
-                          fmul2(t, hh));
+                          fmul2(tt, rs));
         if (MASK) {
           const int q = q0 + col + e + u;  // global query position
           const bool ok0 = (n <= q) && (q < qend) && (n < Tk) && (window <= 0 || q - n < window);
