@@ -408,6 +408,8 @@ def compact_extra(extra):
     c["rope_fwd_TFLOPs"] = {k: v["TFLOP/s"] for k, v in extra["rope_flash_fwd"]["per_shape"].items()}
     c["fp8_vs_bf16_fwd_TFLOPs"] = {k: [v["fp8"]["TFLOP/s"], v["bf16"]["TFLOP/s"]]
                                    for k, v in extra["fp8_flash_fwd"]["per_shape"].items()}
+    c["out_proj_TFLOPs"] = {k: [v["tcgen05"]["TFLOP/s"], v["cublas"]["TFLOP/s"]]
+                            for k, v in extra["out_proj"]["per_shape"].items()}
     if "config1_cpu" in extra:
         c["config1_cpu"] = extra["config1_cpu"]
     return c
@@ -485,6 +487,8 @@ def run_extra(args, world, rank, hbm, tf_burst, tf_sus, peak_kind):
     torch.cuda.empty_cache()
     out["fp8_flash_fwd"] = extra_fp8(FP8_SHAPES, 20, world, g)
     torch.cuda.empty_cache()
+    out["out_proj"] = extra_proj(PROJ_SHAPES, 20, world, g, tf_burst)
+    torch.cuda.empty_cache()
     return out
 
 
@@ -494,6 +498,7 @@ DECODE_SHAPES = ((1, 32, 8, 8192, 128, 16), (1, 32, 8, 32768, 128, 16), (8, 32, 
                  (64, 32, 8, 4096, 128, 16))
 ROPE_SHAPES = ((2, 32, 1024, 128), (4, 12, 512, 64), (2, 32, 8192, 128))  # tests/test_rope_proj.py:162-163 + long
 FP8_SHAPES = ((4, 8, 1024, 64), (2, 32, 8192, 128))  # tests/test_fp8_flash.py:126-127 + long
+PROJ_SHAPES = ((2, 8192, 32, 128, 4096), (4, 2048, 32, 128, 4096))  # B, T, H, D, D_model of the RoPE projection
 CP_SHAPE = (1, 32, 65536, 128)  # one long sequence split over the ranks (context parallelism)
 E2E_CHUNKS = 16  # slices of the e2e step's batch (upload / compute / download pipeline)
 
@@ -632,6 +637,30 @@ def extra_fp8(shapes, steps, world, g):
         del q, k, v
     return {"config": "FP8 (E4M3 QK^T) causal squareplus attention forward incl. quantization, "
                       "public API per call; bf16 forward beside it", "per_shape": f8}
+
+
+def extra_proj(shapes, steps, world, g, tf_burst):
+    """RoPE attention output projection: [B*T, H*D] @ [H*D, D_model] on the
+    tcgen05 GEMM (sa_out_proj), beside cuBLAS (torch.matmul) on the same
+    operands for scale."""
+    import smooth_attn.kernels as K
+
+    dev = torch.device("cuda")
+    res = {}
+    for B, T, H, D, DM in shapes:
+        a = torch.randn(B * T, H * D, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(H * D, DM, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        fl = 2.0 * B * T * H * D * DM
+        row = {}
+        for name, fn in (("tcgen05", lambda: K._out_proj(a, w)), ("cublas", lambda: torch.matmul(a, w))):
+            for _ in range(3):
+                fn()
+            ms = time_steps(fn, steps, world) / steps
+            row[name] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(fl / (ms * 1e-3) / 1e12, 1)}
+        row["frac_of_burst"] = round(row["tcgen05"]["TFLOP/s"] / tf_burst, 3)
+        res[f"M={B * T} K={H * D} N={DM}"] = row
+        del a, w
+    return {"config": "RoPE projection GEMM, bf16 operands, fp32 accumulation", "per_shape": res}
 
 
 CPU_BLOCK_ROWS = 128  # CPU sample unit: a 128-row block of one [2048, 2048] causal matrix

@@ -242,6 +242,22 @@ SA_API int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const
                               float scale, int64_t window_size, int exact_math, int dtype, void* stream);
 
 /*
+ * Output projection of the RoPE attention (or any 16-bit GEMM of this shape):
+ *   out[M, N] = a[M, K] w[K, N],  fp32 accumulation on tcgen05 tensor cores,
+ *   one rounding to the 16-bit output type.
+ * a, w, out row-major with row strides lda, ldw, ldo (elements, multiples of
+ * 8, 16-byte aligned bases); N a multiple of 8; dtype SA_BF16 or SA_F16.
+ * For the RoPE projection a = the attention output laid out [B*T, H*D] and
+ * w = W_o reshaped [H*D, D_model], so the sum over heads is the contraction.
+ *
+ * Replaces: the W_o stage of _sp2norm_rope_flash_proj_fwd_kernel
+ *             (src/smooth_attn/kernels.py:2233-2370), which adds per-head
+ *             bf16 partials with atomic_add.
+ */
+SA_API int sa_out_proj(const void* a, const void* w, void* out, int64_t M, int64_t K, int64_t N, int64_t lda,
+                int64_t ldw, int64_t ldo, int dtype, void* stream);
+
+/*
  * Rotary position embedding, rotate-half form, rounded to the input type:
  *   out[..., i] = x1 c - x2 s,  out[..., i + D/2] = x2 c + x1 s
  * with x1 = x[..., i], x2 = x[..., i + D/2], c = cos[t, i], s = sin[t, i],

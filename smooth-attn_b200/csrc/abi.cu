@@ -20,6 +20,7 @@ int paged_timeouts(int reset, cudaStream_t st);      // paged.cu
 int paged_bad_pages(int reset, cudaStream_t st);     // paged.cu
 int paged_tc_timeouts(int reset, cudaStream_t st);   // paged_tc.cu
 int paged_tc_bad_pages(int reset, cudaStream_t st);  // paged_tc.cu
+int proj_timeouts(int reset, cudaStream_t st);       // proj.cu
 
 // Waits that the probe kernel below gave up on.
 __device__ unsigned g_probe_timeouts;
@@ -56,7 +57,8 @@ __global__ void __launch_bounds__(32) bounded_wait_probe(uint64_t limit_ns, int*
 
 static int collect(int reset, cudaStream_t st) {
   const int n = norm_timeouts(reset, st) + flash_timeouts(reset, st) + flash_bwd_timeouts(reset, st) +
-                paged_timeouts(reset, st) + paged_tc_timeouts(reset, st) + probe_timeouts(reset, st);
+                paged_timeouts(reset, st) + paged_tc_timeouts(reset, st) + probe_timeouts(reset, st) +
+                proj_timeouts(reset, st);
   const int bad = paged_bad_pages(reset, st) + paged_tc_bad_pages(reset, st);
   return n ? SA_ERR_TIMEOUT : bad ? SA_ERR_ARG : SA_OK;
 }

@@ -22,6 +22,7 @@ Outputs never alias inputs.  Ops (namespace ``smooth_attn_b200``):
 ``o_lo`` is the residual of o's 16-bit rounding (empty when not requested);
 the backward ops take an empty ``o_lo`` for "none".
 * ``rope_flash_fwd(q, k, v, cos, sin, scale, window_size) -> o``
+* ``out_proj(a, w) -> a @ w`` (the RoPE projection GEMM)
 * ``fp8_flash_fwd(q, k, v, scale, window_size) -> o``
 * ``paged_decode(q, k_cache, v_cache, block_table, context_lens, scale, block_size) -> out``
 """
@@ -148,6 +149,16 @@ def rope_flash_fwd(q: Tensor, k: Tensor, v: Tensor, cos: Tensor, sin: Tensor, sc
 @rope_flash_fwd.register_fake
 def _(q, k, v, cos, sin, scale, window_size):
     return torch.empty(q.shape, device=q.device, dtype=q.dtype)
+
+
+@torch.library.custom_op(f"{NS}::out_proj", mutates_args=(), device_types="cuda")
+def out_proj(a: Tensor, w: Tensor) -> Tensor:
+    return K._out_proj_direct(a, w)
+
+
+@out_proj.register_fake
+def _(a, w):
+    return torch.empty(a.shape[0], w.shape[1], device=a.device, dtype=a.dtype)
 
 
 @torch.library.custom_op(f"{NS}::fp8_flash_fwd", mutates_args=(), device_types="cuda")

@@ -806,10 +806,10 @@ def sp2norm_rope_flash_attention_proj(q, k, v, w_o, cos, sin, *, scale=None, win
     (kernels.py:2433-2490).
 
     w_o: [H_q, D, D_model].  The attention writes its output straight into a
-    [B, T, H_q, D] buffer, so the projection summed over heads is one plain
-    GEMM [B*T, H_q*D] @ [H_q*D, D_model] with fp32 accumulation (the
-    reference accumulates heads with bf16 atomics).  Returns [B, T, D_model]
-    bf16.
+    [B, T, H_q, D] buffer, so the projection summed over heads is one GEMM
+    [B*T, H_q*D] @ [H_q*D, D_model] on tcgen05 tensor cores (``sa_out_proj``)
+    with fp32 accumulation (the reference accumulates heads with bf16
+    atomics).  Returns [B, T, D_model] bf16.
     """
     assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
     B, H_q, T, D = q.shape
@@ -822,8 +822,35 @@ def sp2norm_rope_flash_attention_proj(q, k, v, w_o, cos, sin, *, scale=None, win
         scale = 1.0 / math.sqrt(D)
     o_bthd = torch.empty(B, T, H_q, D, device=q.device, dtype=q.dtype)
     _rope_flash_fwd(q, k, v, cos, sin, scale, window_size, o=o_bthd.permute(0, 2, 1, 3))
-    w = w_o.to(device=q.device, dtype=q.dtype).reshape(H_q * D, D_model)
-    return torch.matmul(o_bthd.view(B * T, H_q * D), w).view(B, T, D_model).to(torch.bfloat16)
+    w = w_o.to(device=q.device, dtype=q.dtype).reshape(H_q * D, D_model).contiguous()
+    out = _out_proj(o_bthd.view(B * T, H_q * D), w)
+    return out.view(B, T, D_model).to(torch.bfloat16)
+
+
+def _out_proj(a, w):
+    """a [M, K] @ w [K, N] -> [M, N] in a's dtype (``sa_out_proj``)."""
+    if _tracing(a, w):
+        return _ops().out_proj(a, w)
+    return _out_proj_direct(a, w)
+
+
+def _out_proj_direct(a, w):
+    M, K = a.shape
+    N = w.shape[1]
+    out = torch.empty(M, N, device=a.device, dtype=a.dtype)
+    if M == 0 or N == 0:
+        return out
+    if K == 0:
+        return out.zero_()
+    if a.stride(1) != 1 or (a.stride(0) * 2) % 16 or a.data_ptr() % 16:
+        a = a.contiguous()
+    if w.stride(1) != 1 or (w.stride(0) * 2) % 16 or w.data_ptr() % 16:
+        w = w.contiguous()
+    with _on(a.device):
+        st = _lib.load().sa_out_proj(a.data_ptr(), w.data_ptr(), out.data_ptr(), M, K, N, a.stride(0), w.stride(0),
+                                     out.stride(0), _DTYPE_CODE[a.dtype], _stream(a))
+    _lib.check(st, "sa_out_proj")
+    return out
 def _fp8_quantize(q, k, v):
     """Per-tensor E4M3 quantization of q, k, v on the device (sa_fp8_quantize;
     the reference's _quantize_to_fp8, kernels.py:2592-2601, without its

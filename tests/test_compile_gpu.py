@@ -99,6 +99,7 @@ def test_opcheck_all_ops():
                                lo[:, :, 64:].contiguous(), do[:, :, 64:].contiguous(),
                                rs[:, :, 64:].contiguous(), 64, 0.125, 0, False)),
         (OPS.rope_flash_fwd, (q, k, v, cos, sin, 0.125, 0)),
+        (OPS.out_proj, (q.view(-1, 64)[:192], randn((64, 40), 11, torch.bfloat16, CUDA))),
         (OPS.fp8_flash_fwd, (q, k, v, 0.125, 0)),
         (OPS.paged_decode, (qd, kc, vc, bt, cl, 0.125, 16)),
     ]
