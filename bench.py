@@ -694,6 +694,45 @@ def _cpu_norm_sample(seconds, threads, min_batches=1):
     return nbytes, time.perf_counter() - t0
 
 
+def cpu_config1(reps=20):
+    """BASELINE configs[0] timed in full on the host: causal squareplus norm of
+    fp32 [2,8,128,128] N(0,1) scores (alpha 2, theta 0.5, power 2), forward and
+    forward + eager autograd backward with an N(0,1) upstream gradient, through
+    the reference's eager algorithm in torch (``softplus_norm_causal_eager``:
+    the activation, the cached triu mask, masked_fill, the row sum + 1e-12,
+    src/smooth_attn/kernels.py:1349-1365) on all host threads, and through the
+    numpy port for comparison.  Median of ``reps`` runs after 3 warm-ups."""
+    import smooth_attn as sa
+    from oracle import sa_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(1234)
+    x = torch.randn(2, 8, 128, 128, generator=g)
+    dy = torch.randn(2, 8, 128, 128, generator=g)
+
+    def med(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return round(statistics.median(ts) * 1e6, 1)
+
+    def fwd_bwd():
+        xr = x.clone().requires_grad_(True)
+        sa.softplus_norm_causal_eager(xr).backward(dy)
+
+    xn, dyn = x.numpy(), dy.numpy()
+    return {"config": "BASELINE configs[0]: fp32 [2,8,128,128], alpha 2, theta 0.5, power 2",
+            "torch_eager_fwd_us": med(lambda: sa.softplus_norm_causal_eager(x)),
+            "torch_eager_fwd_bwd_us": med(fwd_bwd),
+            "numpy_port_fwd_us": med(lambda: O.softplus_norm_causal(xn)),
+            "numpy_port_fwd_bwd_us": med(lambda: (O.softplus_norm_causal(xn), O.softplus_norm_causal_bwd(xn, dyn))),
+            "threads": torch.get_num_threads()}
+
+
 def cpu_baseline(seconds=10.0):
     threads = os.cpu_count() or 1
     nbytes, dt = _cpu_norm_sample(seconds, threads)
@@ -701,7 +740,8 @@ def cpu_baseline(seconds=10.0):
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{nbytes / norm_bytes(1, NORM_CFG['L']):.1f} matrix-equivalents of [2048,2048] as 128-row "
                       f"blocks (numpy oracle, fp32 math, bf16-sized bytes), "
-                      f"{dt:.1f} s, {threads} threads"}
+                      f"{dt:.1f} s, {threads} threads",
+            "config1": cpu_config1()}
 
 
 def run_reference(args):
@@ -733,6 +773,7 @@ def run_reference(args):
                                    f"median step"},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    line["cpu_baseline"]["config1"] = cpu_config1()
     print(json.dumps(line), flush=True)
 
 
