@@ -163,6 +163,12 @@ SA_API int64_t sa_flash_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, i
  * sa_flash_bwd_workspace_size() bytes, 256 B aligned, contents undefined on
  * entry.  sa_flash_bwd_workspace_size() returns 0 for sizes whose byte
  * count overflows int64; such problems are rejected.
+ * deterministic = 0: dQ is accumulated by the key-major kernel with fp32
+ * atomics (fastest; the order of the adds, and so dQ's last bits, varies
+ * from run to run).  deterministic != 0: the key-major kernel computes dK and
+ * dV only and a query-major kernel sums each dQ row over the key tiles in a
+ * fixed order inside one CTA (the reference's order, kernels.py:1680-1784):
+ * bitwise reproducible, at the cost of recomputing S and dP once more.
  *
  * Replaces: _sp2norm_flash_bwd, _sp2norm_flash_bwd_dq_kernel,
  *           _sp2norm_flash_bwd_dkv_kernel
@@ -175,6 +181,7 @@ SA_API int sa_flash_bwd(const void* q, const void* k, const void* v, const void*
                  const int64_t* k_strides, const int64_t* v_strides, const int64_t* o_strides,
                  const int64_t* do_strides, const int64_t* dq_strides, const int64_t* dk_strides,
                  const int64_t* dv_strides, float scale, int64_t window_size, int exact_math, int dtype,
+                 int deterministic,
                  void* stream);
 
 /*
@@ -239,7 +246,8 @@ SA_API int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, const
                               int64_t q_offset, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
                               const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
                               const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
-                              float scale, int64_t window_size, int exact_math, int dtype, void* stream);
+                              float scale, int64_t window_size, int exact_math, int dtype,
+                              int deterministic, void* stream);
 
 /*
  * Output projection of the RoPE attention (or any 16-bit GEMM of this shape):

@@ -203,7 +203,7 @@ struct BwdBars {
   uint32_t tmem_base;
 };
 
-template <int D, bool BF16, bool EXACT>
+template <int D, bool BF16, bool EXACT, bool WITH_DQ = true>
 __global__ void __launch_bounds__(192, 1)
     sp2_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int it = 0; it < ntiles; ++it) {
           const int st = it & 1;
           if (!b_wait(&bars->qdo_full[st], (it >> 1) & 1, failed)) break;
-          if (it > 0 && !b_wait(&bars->dq_free, (it - 1) & 1, failed)) break;
+          if (WITH_DQ && it > 0 && !b_wait(&bars->dq_free, (it - 1) & 1, failed)) break;
           tc_fence_after();
           const uint32_t q_s = aQ + st * C::TILE, do_s = aDO + st * C::TILE;
 #pragma unroll
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(192, 1)
           }
           // dQ = dS K   (M = query rows, K = 128 KV rows)
 #pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk) {
+          for (int kk = 0; kk < (WITH_DQ ? C::BN / 16 : 0); ++kk) {
             const uint64_t a_ds = smem_desc(aDS + kk * 16 * 128, 128 * 128, 1024, SW_128B);
             const uint64_t b_k = smem_desc(aK + kk * 16 * C::ROWB, 128 * C::ROWB, C::SBO, C::SWZ);
             mma_ss(tP, a_ds, b_k, id_dq, kk > 0);
@@ -382,6 +382,7 @@ __global__ void __launch_bounds__(192, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ds_ready);
+      if (!WITH_DQ) continue;  // dQ comes from the query-major kernel
       // drain dQ (TMEM lane = query row) with fp32 vector atomics
       if (!b_warp_wait(&bars->mm2_done, it & 1, failed)) break;
       tc_fence_after();
@@ -574,7 +575,7 @@ __device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, u
   }
 }
 
-template <bool BF16, bool EXACT>
+template <bool BF16, bool EXACT, bool WITH_DQ = true>
 __global__ void __launch_bounds__(448, 1)
     sp2_bwd128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
@@ -736,7 +737,7 @@ __global__ void __launch_bounds__(448, 1)
             mma_ss(tDK, desc_add(ads0, kk * 32), desc_add(bq0, kk * 16 * 128), id_kv, (it > 0 || kk > 0) ? 1u : 0u);
           }
 #pragma unroll
-          for (int kk = 0; kk < C::BN / 16; ++kk) {  // dQ^T = K^T dS^T into dP^T buffer bb (consumed)
+          for (int kk = 0; kk < (WITH_DQ ? C::BN / 16 : 0); ++kk) {  // dQ^T = K^T dS^T into dP^T buffer bb (consumed)
             mma_ss(tbase + 128 + bb * 64, desc_add(dKt0, kk * 16 * 128), desc_add(bds0, kk * 16 * 128), id_dq, kk > 0);
           }
           mma_commit(&bars->mm2_done[bb]);
@@ -748,7 +749,7 @@ __global__ void __launch_bounds__(448, 1)
             // S^T(nx) overwrites the columns dV(it) reads P from: tcgen05.mma
             // ops of one thread execute in issue order, so no wait is needed.
             issue_s(nx);
-            if (!b_wait(&bars->dq_free, it & 1, failed)) break;
+            if (WITH_DQ && !b_wait(&bars->dq_free, it & 1, failed)) break;
             tc_fence_after();
             issue_dp(nx);
           }
@@ -762,7 +763,7 @@ __global__ void __launch_bounds__(448, 1)
     const int d = 32 * g + lane;  // TMEM lane = head-dim index of dQ^T
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     Cursor cur{kvh * G, qt_first};
-    for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
+    for (int it = 0; it < (WITH_DQ ? ntiles : 0) && !failed; ++it, advance(cur)) {
       // polling (not suspending): the drain's reaction time gates the next dP^T
       if (!b_warp_wait_spin(&bars->mm2_done[it & 1], (it >> 1) & 1, failed)) break;
       tc_fence_after();
@@ -883,6 +884,347 @@ __global__ void __launch_bounds__(448, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Deterministic dQ: one CTA per 128-row query tile of one (batch, query head),
+// the reference's query-major order (src/smooth_attn/kernels.py:1680-1784).
+// Every dQ element is summed inside one CTA's TMEM accumulator over the key
+// tiles in a fixed order and written once, so the result is bitwise the same
+// run to run (the key-major kernel's fp32 atomics are not).  Per key tile j:
+//   S_j = Q K_j^T  (TMEM, double-buffered),  dP_j = dO V_j^T  (TMEM),
+//   elementwise (thread = query row, 1/R and delta folded into registers):
+//   dS = (dP scale/R - delta scale/R) * t^2 rsqrt(a^2+4), rounded to 16 bits
+//   over S_j's own columns (the forward's P layout),
+//   dQ += dS K_j  (A = dS from TMEM, B = K_j as an N-major operand).
+// dP_{j+1} is issued as soon as the elementwise warps have read dP_j into
+// registers, and S_{j+2} right after dQ_j, so the tensor pipe runs under the
+// elementwise stage.  TMEM: S_0 @0, S_1 @128, dP @256, dQ @384 (D columns).
+// Warps 0-7: elementwise (two warpgroups, 64 key columns each); warp 8: TMA;
+// warp 9: MMA.
+// ---------------------------------------------------------------------------
+template <int D>
+struct DqCfg {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int CHUNK = D >= 64 ? 64 : D;  // elements per swizzled smem row
+  static constexpr int NCHUNK = D / CHUNK;
+  static constexpr int ROWB = CHUNK * 2;
+  static constexpr uint32_t SWZ = ROWB == 128 ? SW_128B : SW_64B;
+  static constexpr int SBO = 8 * ROWB;
+  static constexpr int TILE = 128 * D * 2;  // one Q / dO / K / V tile
+  static constexpr int NK = 3, NV = 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = OFF_Q + TILE;
+  static constexpr int OFF_K = OFF_DO + TILE;
+  static constexpr int OFF_V = OFF_K + NK * TILE;
+  static constexpr int OFF_BAR = OFF_V + NV * TILE;
+  // at least half an SM's shared memory: one CTA per SM, so a second CTA
+  // never waits in tcgen05.alloc for the first one's 512 TMEM columns
+  static constexpr int SMEM = OFF_BAR + 512 + 1024 > 116 * 1024 ? OFF_BAR + 512 + 1024 : 116 * 1024;
+  static constexpr int THREADS = 320;
+  static_assert(SMEM <= 227 * 1024, "shared memory plan");
+};
+
+struct DqBars {
+  uint64_t q_full;
+  uint64_t k_full[3], k_empty[3];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[2];   // S_j ready in buffer j & 1
+  uint64_t dp_full;     // dP_j ready
+  uint64_t dp_read;     // dP_j read into registers (256 arrivals): the buffer is free
+  uint64_t ds_full[2];  // dS_j written over S buffer j & 1 (256 arrivals)
+  uint64_t dq_full;
+  uint32_t tmem_base;
+};
+
+struct DqParams {
+  void* dq;
+  const float* rowsum;  // R  [B, Hq, T]
+  const float* delta;   // [B, Hq, T]
+  int64_t sdq_b, sdq_h, sdq_s;
+  int B, Hq, Hkv, T, ntiles, window;
+  int Tk, qoff;
+  float scale;
+};
+
+// KV tile range [j0, j1) seen by the 128 query rows at local row q0.
+__device__ __forceinline__ void dq_kv_range(int q0, int Tq, int qoff, int Tk, int window, int& j0, int& j1) {
+  const int q0g = q0 + qoff;
+  const int nkv = (Tk + 127) / 128;
+  j1 = (q0g + 128 + 127) / 128;
+  if (j1 > nkv) j1 = nkv;
+  j0 = 0;
+  if (window > 0) {
+    const int first = q0g - window + 1;
+    j0 = first > 0 ? first / 128 : 0;
+  }
+  if (q0 >= Tq || j1 < j0) j1 = j0;
+}
+
+// dS for 32 key columns of one query row already in registers (s: scores,
+// g: dP); writes the 16-bit dS pairs (16 columns) at taddr and taddr + 8.
+template <bool BF16, bool EXACT, bool MASK>
+__device__ __forceinline__ void dq_ds32(const uint32_t (&s)[32], const uint32_t (&g)[32], uint32_t taddr,
+                                        float scale2, float cs, float ncd, int kbase, int q, int Tk, int window) {
+  uint32_t pk[16];
+  const float2 sc2 = make_float2(scale2, scale2), m1 = make_float2(-1.0f, -1.0f), four = make_float2(4.0f, 4.0f);
+  const float2 cs2 = make_float2(cs, cs), ncd2 = make_float2(ncd, ncd);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float2 a = ffma2(make_float2(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1])), sc2, m1);
+    const float2 w = ffma2(a, a, four);
+    const float2 rs = make_float2(rsqrt_approx(w.x), rsqrt_approx(w.y));
+    const float2 t = EXACT ? make_float2(a.x + sqrtf(w.x), a.y + sqrtf(w.y)) : ffma2(w, rs, a);
+    // 4 sp sp' = t^2 rsqrt(w); dS = (dP scale/R - delta scale/R) * 4 sp sp'
+    float2 ds = fmul2(ffma2(make_float2(__uint_as_float(g[2 * k]), __uint_as_float(g[2 * k + 1])), cs2, ncd2),
+                      fmul2(fmul2(t, t), rs));
+    if (MASK) {
+      const int kk = kbase + 2 * k;
+      const bool ok0 = (kk <= q) && (kk < Tk) && (window <= 0 || q - kk < window);
+      const bool ok1 = (kk + 1 <= q) && (kk + 1 < Tk) && (window <= 0 || q - kk - 1 < window);
+      ds.x = ok0 ? ds.x : 0.f;
+      ds.y = ok1 ? ds.y : 0.f;
+    }
+    pk[k] = BF16 ? pack2_bf16(ds.x, ds.y) : pack2_f16(ds.x, ds.y);
+  }
+  tmem_st8(taddr, *reinterpret_cast<const uint32_t(*)[8]>(&pk[0]));
+  tmem_st8(taddr + 8, *reinterpret_cast<const uint32_t(*)[8]>(&pk[8]));
+}
+
+template <int D, bool BF16, bool EXACT>
+__global__ void __launch_bounds__(320, 1)
+    sp2_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                      const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
+                      DqParams p) {
+  using C = DqCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sDO = smem + C::OFF_DO;
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  DqBars* bars = reinterpret_cast<DqBars*>(smem + C::OFF_BAR);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int xr, bh;
+  grouped_longest_first((int)blockIdx.x, p.ntiles, p.B * p.Hq, kHeadGroup, xr, bh);
+  const int qt = p.ntiles - 1 - xr;  // x = 0: the tile with the most key tiles
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int q0 = qt * C::BM;
+  int j0, j1;
+  dq_kv_range(q0, p.T, p.qoff, p.Tk, p.window, j0, j1);
+  const int n = j1 - j0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->ds_full[i], 256);
+    }
+    mbar_init(&bars->dp_full, 1);
+    mbar_init(&bars->dp_read, 256);
+    mbar_init(&bars->dq_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  bool failed = false;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    // order of need: K_0, V_0, K_1, then V_{j+1} and K_{j+2} for j = 0, 1, ...
+    if (elect_one()) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      tma_prefetch_desc(&tmdo);
+      if (n > 0) mbar_arrive_expect_tx(&bars->q_full, 2 * C::TILE);  // no copy in flight when there is no work
+      for (int c = 0; c < (n > 0 ? C::NCHUNK : 0); ++c) {
+        tma_load_4d(sQ + c * 128 * C::ROWB, &tmq, c * C::CHUNK, q0, h, b, &bars->q_full);
+        tma_load_4d(sDO + c * 128 * C::ROWB, &tmdo, c * C::CHUNK, q0, h, b, &bars->q_full);
+      }
+      auto load_k = [&](int i) {
+        const int ks = i % C::NK;
+        if (i >= C::NK && !b_wait(&bars->k_empty[ks], ((i / C::NK) - 1) & 1, failed)) return;
+        mbar_arrive_expect_tx(&bars->k_full[ks], C::TILE);
+        for (int c = 0; c < C::NCHUNK; ++c)
+          tma_load_4d(sK + ks * C::TILE + c * 128 * C::ROWB, &tmk, c * C::CHUNK, (j0 + i) * C::BN, kvh, b,
+                      &bars->k_full[ks]);
+      };
+      auto load_v = [&](int i) {
+        const int vs = i % C::NV;
+        if (i >= C::NV && !b_wait(&bars->v_empty[vs], ((i / C::NV) - 1) & 1, failed)) return;
+        mbar_arrive_expect_tx(&bars->v_full[vs], C::TILE);
+        for (int c = 0; c < C::NCHUNK; ++c)
+          tma_load_4d(sV + vs * C::TILE + c * 128 * C::ROWB, &tmv, c * C::CHUNK, (j0 + i) * C::BN, kvh, b,
+                      &bars->v_full[vs]);
+      };
+      if (n > 0) load_k(0);
+      if (n > 0) load_v(0);
+      if (n > 1) load_k(1);
+      for (int j = 0; j < n && !failed; ++j) {
+        if (j + 1 < n) load_v(j + 1);
+        if (j + 2 < n) load_k(j + 2);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr int ab = BF16 ? 1 : 0;
+      constexpr uint32_t id_sp = idesc_f16(128, C::BN, ab, 0, 0);  // S, dP: A, B K-major
+      constexpr uint32_t id_dq = idesc_f16(128, D, ab, 0, 1);      // dQ: A (dS, TMEM), B = K N-major
+      const uint64_t dQ0 = smem_desc(smem_u32(sQ), 16, C::SBO, C::SWZ);
+      const uint64_t dDO0 = smem_desc(smem_u32(sDO), 16, C::SBO, C::SWZ);
+      const uint64_t dK0 = smem_desc(smem_u32(sK), 16, C::SBO, C::SWZ);
+      const uint64_t dV0 = smem_desc(smem_u32(sV), 16, C::SBO, C::SWZ);
+      const uint64_t dKn0 = smem_desc(smem_u32(sK), 128 * C::ROWB, C::SBO, C::SWZ);  // K as N-major B
+      auto gemm_kmajor = [&](uint32_t dst, uint64_t a0, uint64_t b0) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk * 16) / C::CHUNK) * 128 * C::ROWB + ((kk * 16) % C::CHUNK) * 2;
+          mma_ss(dst, desc_add(a0, off), desc_add(b0, off), id_sp, kk > 0);
+        }
+      };
+      auto issue_s = [&](int i) {
+        const int ks = i % C::NK;
+        if (!b_wait(&bars->k_full[ks], (i / C::NK) & 1, failed)) return;
+        tc_fence_after();
+        gemm_kmajor(tbase + (i & 1) * 128, dQ0, desc_add(dK0, ks * C::TILE));
+        mma_commit(&bars->s_full[i & 1]);
+      };
+      auto issue_dp = [&](int i) {
+        const int vs = i % C::NV;
+        if (!b_wait(&bars->v_full[vs], (i / C::NV) & 1, failed)) return;
+        tc_fence_after();
+        gemm_kmajor(tbase + 256, dDO0, desc_add(dV0, vs * C::TILE));
+        mma_commit(&bars->dp_full);
+        mma_commit(&bars->v_empty[vs]);
+      };
+      if (n > 0 && b_wait(&bars->q_full, 0, failed)) {
+        issue_s(0);
+        issue_dp(0);
+        if (n > 1) issue_s(1);
+        for (int j = 0; j < n && !failed; ++j) {
+          const int sb = j & 1;
+          if (j + 1 < n) {
+            // dP_{j+1} into the one dP buffer once dP_j is in the elementwise warps' registers
+            if (!b_wait(&bars->dp_read, j & 1, failed)) break;
+            issue_dp(j + 1);
+          }
+          if (!b_wait(&bars->ds_full[sb], (j >> 1) & 1, failed)) break;
+          tc_fence_after();
+          const uint64_t dk = desc_add(dKn0, (j % C::NK) * C::TILE);
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk)
+            mma_ts(tbase + 384, tbase + sb * 128 + (kk >> 1) * 32 + (kk & 1) * 8, desc_add(dk, kk * 16 * C::ROWB),
+                   id_dq, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&bars->k_empty[j % C::NK]);
+          // S_{j+2} reuses the buffer dQ_j reads dS_j from: tcgen05.mma ops of
+          // one thread execute in issue order
+          if (j + 2 < n) issue_s(j + 2);
+        }
+      }
+      mma_commit(&bars->dq_full);  // also when there was no work
+    }
+  } else {
+    // ------------------------------------------------------------ elementwise warps
+    const int hf = warp >> 2;  // key-column half
+    const int g = warp & 3;
+    const int row = 32 * g + lane;
+    const int q = q0 + row;
+    const int q0g = q0 + p.qoff, qg = q + p.qoff;
+    const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
+    const float scale2 = 2.0f * p.scale;
+    float cs = 0.f, ncd = 0.f;
+    if (q < p.T) {
+      const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + q;
+      const float ir = 1.0f / __ldg(p.rowsum + idx);
+      cs = p.scale * ir;
+      ncd = -(__ldg(p.delta + idx) * p.scale * ir);
+    }
+    for (int j = 0; j < n; ++j) {
+      const int sb = j & 1;
+      if (!b_warp_wait(&bars->dp_full, j & 1, failed)) break;
+      tc_fence_after();
+      uint32_t gd[64];
+      tmem_ld32(tl + 256 + hf * 64, *reinterpret_cast<uint32_t(*)[32]>(&gd[0]));
+      tmem_ld32(tl + 256 + hf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&gd[32]));
+      tmem_ld_wait_n(gd);
+      tc_fence_before();
+      mbar_arrive(&bars->dp_read);
+      if (!b_warp_wait(&bars->s_full[sb], (j >> 1) & 1, failed)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int col = hf * 64 + 32 * c;  // first score column of this 32-column chunk
+        const int kc = (j0 + j) * C::BN + col;
+        const bool need_mask = (kc + 31 > q0g) || (kc + 32 > p.Tk) ||
+                               (p.window > 0 && q0g + C::BM - 1 - kc >= p.window) || q0 + C::BM > p.T;
+        // need_mask is the same for the whole warp: dq_ds32's tcgen05.st is
+        // a warp-collective (.sync.aligned) and must not run diverged
+        uint32_t sv[32];
+        tmem_ld32(tl + sb * 128 + col, sv);
+        tmem_ld_wait(sv);
+        // dS of keys [col, col + 32) -> columns 32 (m / 2) + 8 (m % 2) for the
+        // two 16-key slices m = col / 16, col / 16 + 1: inside this chunk's
+        // own, already-read first 16 columns
+        const uint32_t tds = tl + sb * 128 + col;
+        const uint32_t(&gc)[32] = *reinterpret_cast<const uint32_t(*)[32]>(&gd[32 * c]);
+        if (need_mask)
+          dq_ds32<BF16, EXACT, true>(sv, gc, tds, scale2, cs, ncd, kc, q < p.T ? qg : -1, p.Tk, p.window);
+        else
+          dq_ds32<BF16, EXACT, false>(sv, gc, tds, scale2, cs, ncd, 0, 0, 0, 0);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->ds_full[sb]);
+    }
+    if (b_warp_wait(&bars->dq_full, 0, failed) && n > 0) {
+      tc_fence_after();
+      const bool live = q < p.T;
+      uint8_t* drow = static_cast<uint8_t*>(p.dq) + 2 * ((int64_t)b * p.sdq_b + (int64_t)h * p.sdq_h + (int64_t)q * p.sdq_s);
+#pragma unroll 1
+      for (int c = hf * (D / 32); c < (hf + 1) * (D / 32); ++c) {  // this half's D/2 columns, 16 at a time
+        uint32_t r[16];
+        tmem_ld16(tl + 384 + c * 16, r);
+        tmem_ld_wait(r);
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2)
+          pk[e / 2] = BF16 ? pack2_bf16(__uint_as_float(r[e]), __uint_as_float(r[e + 1]))
+                           : pack2_f16(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+        if (live) {
+          uint4* dst = reinterpret_cast<uint4*>(drow + c * 32);
+          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+    } else if (n == 0 && !failed && q < p.T) {  // no visible key: dq = 0
+      uint8_t* drow = static_cast<uint8_t*>(p.dq) + 2 * ((int64_t)b * p.sdq_b + (int64_t)h * p.sdq_h + (int64_t)q * p.sdq_s);
+      for (int c = hf * (D / 16); c < (hf + 1) * (D / 16); ++c)
+        reinterpret_cast<uint4*>(drow)[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 // delta = rowsum(dO * O) (fp32) and dq_acc = 0.  One warp per query row.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) sp2_bwd_prep(const T* __restrict__ o, const T* __restrict__ o_lo,
@@ -935,6 +1277,7 @@ __global__ void __launch_bounds__(256) sp2_bwd_prep(const T* __restrict__ o, con
       delta[r0] = acc0;
       if (two) delta[r1] = acc1;
     }
+    if (dq_acc == nullptr) continue;  // deterministic path: no accumulator
     const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int i = sub; i < D / 4; i += LPR) {
@@ -971,8 +1314,9 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
                       int64_t Hq, int64_t Hkv, int64_t T, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                       const int64_t* os, const int64_t* dos, const int64_t* dqs, const int64_t* dks,
                       const int64_t* dvs, float scale, int64_t window, cudaStream_t st, int64_t Tk = -1,
-                      int64_t qoff = 0) {
+                      int64_t qoff = 0, bool det = false) {
   using C = BwdCfg<D>;
+  if (det) dq_acc = nullptr;  // dQ comes from the query-major kernel: no accumulator
   if (Tk < 0) Tk = T;
   if (((Tk + C::BN - 1) / C::BN) * B * Hkv > INT32_MAX) return SA_ERR_UNSUPPORTED;  // 1-D grid, before any launch
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -1014,13 +1358,37 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
     if (!make_map_4d(&mq64, q, BF16, B, Hq, T, D, qs, 64, Bwd128::BQ) ||
         !make_map_4d(&mdo64, dout, BF16, B, Hq, T, D, dos, 64, Bwd128::BQ))
       return SA_ERR_ALIGN;
-    auto kern = sp2_bwd128_kernel<BF16, EXACT>;
+    auto kern = det ? sp2_bwd128_kernel<BF16, EXACT, false> : sp2_bwd128_kernel<BF16, EXACT, true>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Bwd128::SMEM);
     kern<<<grid, Bwd128::THREADS, Bwd128::SMEM, st>>>(mq64, mk, mv, mdo64, p);
   } else {
-    auto kern = sp2_bwd_kernel<D, BF16, EXACT>;
+    auto kern = det ? sp2_bwd_kernel<D, BF16, EXACT, false> : sp2_bwd_kernel<D, BF16, EXACT, true>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     kern<<<grid, 192, C::SMEM, st>>>(mq, mk, mv, mdo, p);
+  }
+  if (det) {
+    using DC = DqCfg<D>;
+    DqParams dp;
+    dp.dq = dq;
+    dp.rowsum = rowsum;
+    dp.delta = delta;
+    dp.sdq_b = dqs[0];
+    dp.sdq_h = dqs[1];
+    dp.sdq_s = dqs[2];
+    dp.B = (int)B;
+    dp.Hq = (int)Hq;
+    dp.Hkv = (int)Hkv;
+    dp.T = (int)T;
+    dp.Tk = (int)Tk;
+    dp.qoff = (int)qoff;
+    dp.window = (int)window;
+    dp.scale = scale;
+    dp.ntiles = (int)((T + DC::BM - 1) / DC::BM);
+    if ((int64_t)dp.ntiles * B * Hq > INT32_MAX) return SA_ERR_UNSUPPORTED;
+    auto kq = sp2_bwd_dq_kernel<D, BF16, EXACT>;
+    cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, DC::SMEM);
+    kq<<<(unsigned)(dp.ntiles * B * Hq), DC::THREADS, DC::SMEM, st>>>(mq, mk, mv, mdo, dp);
+    return SA_OK;
   }
   const int64_t nthreads = rows * (D / 8);
   sp2_bwd_dq_convert<T16, D><<<(unsigned)((nthreads + 255) / 256), 256, 0, st>>>(
@@ -1074,7 +1442,7 @@ extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const v
                             const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
                             const int64_t* o_strides, const int64_t* do_strides, const int64_t* dq_strides,
                             const int64_t* dk_strides, const int64_t* dv_strides, float scale, int64_t window_size,
-                            int exact_math, int dtype, void* stream) {
+                            int exact_math, int dtype, int deterministic, void* stream) {
   if (dtype != SA_BF16 && dtype != SA_F16) return SA_ERR_UNSUPPORTED;
   if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
   if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Hq % Hkv != 0 || window_size < 0) return SA_ERR_ARG;
@@ -1099,7 +1467,7 @@ extern "C" int sa_flash_bwd(const void* q, const void* k, const void* v, const v
 #define SA_BWD_CASE(DD, BF, EX)                                                                                  \
   rc = launch_bwd<DD, BF, EX>(q, k, v, o, o_lo, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, T, q_strides,     \
                               k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, \
-                              scale, window_size, st)
+                              scale, window_size, st, -1, 0, deterministic != 0)
 #define SA_BWD_D(DD)                              \
   if (dtype == SA_BF16) {                         \
     if (exact_math) SA_BWD_CASE(DD, true, true);  \
@@ -1128,7 +1496,7 @@ extern "C" int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, c
                                   int64_t q_offset, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
                                   const int64_t* v_strides, const int64_t* o_strides, const int64_t* do_strides,
                                   const int64_t* dq_strides, const int64_t* dk_strides, const int64_t* dv_strides,
-                                  float scale, int64_t window_size, int exact_math, int dtype, void* stream) {
+                                  float scale, int64_t window_size, int exact_math, int dtype, int deterministic, void* stream) {
   if (dtype != SA_BF16 && dtype != SA_F16) return SA_ERR_UNSUPPORTED;
   if (D != 32 && D != 64 && D != 128) return SA_ERR_UNSUPPORTED;
   if (B < 0 || Hq < 1 || Hkv < 1 || Tq < 0 || Tk < 0 || q_offset < 0 || Hq % Hkv != 0 || window_size < 0)
@@ -1154,7 +1522,7 @@ extern "C" int sa_flash_bwd_chunk(const void* q, const void* k, const void* v, c
 #define SA_BWDC_CASE(DD, BF, EX)                                                                                 \
   rc = launch_bwd<DD, BF, EX>(q, k, v, o, o_lo, dout, rowsum, dq, dk, dv, dq_acc, delta, B, Hq, Hkv, Tq, q_strides,   \
                               k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides, \
-                              scale, window_size, st, Tk, q_offset)
+                              scale, window_size, st, Tk, q_offset, deterministic != 0)
 #define SA_BWDC_D(DD)                              \
   if (dtype == SA_BF16) {                          \
     if (exact_math) SA_BWDC_CASE(DD, true, true);  \
@@ -1256,5 +1624,5 @@ extern "C" int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v,
   }
   return sa_flash_bwd(q, k, v, o, o_lo, dout, rowsum, dq, dk, dv, scratch, SA_NOALLOC_SCRATCH_BYTES, B, Hq, Hkv, T, D,
                       q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides,
-                      scale, window_size, exact_math, dtype, stream);
+                      scale, window_size, exact_math, dtype, 0, stream);
 }

@@ -51,13 +51,13 @@ SIGNATURES = {
     "sa_flash_bwd": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
                             _i64, _i64, _i64, _i64, _i64,
                             _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
-                            _f, _i64, _int, _int, _p]),
+                            _f, _i64, _int, _int, _int, _p]),
     "sa_flash_fwd_chunk": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                   _i64p, _i64p, _i64p, _i64p, _f, _i64, _int, _int, _p]),
     "sa_flash_bwd_chunk": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
                                   _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                   _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p, _i64p,
-                                  _f, _i64, _int, _int, _p]),
+                                  _f, _i64, _int, _int, _int, _p]),
     "sa_out_proj": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p]),
     "sa_rope_rotate": (_int, [_p, _p, _p, _p, _int, _i64, _i64, _i64, _i64, _i64p, _int, _p]),
     "sa_rope_flash_fwd_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64]),

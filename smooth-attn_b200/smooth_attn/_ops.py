@@ -15,9 +15,10 @@ Outputs never alias inputs.  Ops (namespace ``smooth_attn_b200``):
 * ``norm_fwd(x, alpha, theta, power, causal, with_rowsum) -> (out, rowsum)``
 * ``norm_causal_bwd(x, g, rowsum, alpha, theta, power) -> dx``
 * ``flash_fwd(q, k, v, scale, window_size, use_fast_sqrt, with_residual) -> (o, row_sums, o_lo)``
-* ``flash_bwd(q, k, v, o, o_lo, do, row_sums, scale, window_size, use_fast_sqrt) -> (dq, dk, dv)``
+* ``flash_bwd(q, k, v, o, o_lo, do, row_sums, scale, window_size, use_fast_sqrt, deterministic) -> (dq, dk, dv)``
 * ``flash_fwd_chunk(q, k, v, q_offset, scale, window_size, exact_math, with_residual) -> (o, row_sums, o_lo)``
-* ``flash_bwd_chunk(q, k, v, o, o_lo, do, row_sums, q_offset, scale, window_size, exact_math) -> (dq, dk, dv)``
+* ``flash_bwd_chunk(q, k, v, o, o_lo, do, row_sums, q_offset, scale, window_size, exact_math, deterministic)
+  -> (dq, dk, dv)``
 
 ``o_lo`` is the residual of o's 16-bit rounding (empty when not requested);
 the backward ops take an empty ``o_lo`` for "none".
@@ -102,14 +103,14 @@ def _(q, k, v, scale, window_size, use_fast_sqrt, with_residual):
 
 @torch.library.custom_op(f"{NS}::flash_bwd", mutates_args=(), device_types="cuda")
 def flash_bwd(q: Tensor, k: Tensor, v: Tensor, o: Tensor, o_lo: Tensor, do: Tensor, row_sums: Tensor, scale: float,
-              window_size: int, use_fast_sqrt: bool) -> tuple[Tensor, Tensor, Tensor]:
+              window_size: int, use_fast_sqrt: bool, deterministic: bool) -> tuple[Tensor, Tensor, Tensor]:
     q, k, v, o = (K._flash_ready(t) for t in (q, k, v, o))
     return K._flash_bwd_direct(q, k, v, o, do, row_sums.contiguous(), scale, window_size, use_fast_sqrt,
-                               o_lo=o_lo if o_lo.numel() else None)
+                               o_lo=o_lo if o_lo.numel() else None, deterministic=deterministic)
 
 
 @flash_bwd.register_fake
-def _(q, k, v, o, o_lo, do, row_sums, scale, window_size, use_fast_sqrt):
+def _(q, k, v, o, o_lo, do, row_sums, scale, window_size, use_fast_sqrt, deterministic):
     return tuple(torch.empty(t.shape, device=q.device, dtype=q.dtype) for t in (q, k, v))
 
 
@@ -130,13 +131,14 @@ def _(q, k, v, q_offset, scale, window_size, exact_math, with_residual):
 
 @torch.library.custom_op(f"{NS}::flash_bwd_chunk", mutates_args=(), device_types="cuda")
 def flash_bwd_chunk(q: Tensor, k: Tensor, v: Tensor, o: Tensor, o_lo: Tensor, do: Tensor, row_sums: Tensor,
-                    q_offset: int, scale: float, window_size: int, exact_math: bool) -> tuple[Tensor, Tensor, Tensor]:
+                    q_offset: int, scale: float, window_size: int, exact_math: bool,
+                    deterministic: bool) -> tuple[Tensor, Tensor, Tensor]:
     return K._flash_bwd_chunk_direct(q, k, v, o, do, row_sums.contiguous(), q_offset, scale, window_size,
-                                     exact_math, o_lo if o_lo.numel() else None)
+                                     exact_math, o_lo if o_lo.numel() else None, deterministic)
 
 
 @flash_bwd_chunk.register_fake
-def _(q, k, v, o, o_lo, do, row_sums, q_offset, scale, window_size, exact_math):
+def _(q, k, v, o, o_lo, do, row_sums, q_offset, scale, window_size, exact_math, deterministic):
     return tuple(torch.empty(t.shape, device=q.device, dtype=q.dtype) for t in (q, k, v))
 
 

@@ -549,18 +549,28 @@ def _match_strides(o_lo, o):
     return torch.empty_strided(o.shape, o.stride(), device=o.device, dtype=o.dtype).copy_(o_lo)
 
 
+def _deterministic(flag):
+    """None follows torch.use_deterministic_algorithms(); otherwise the flag."""
+    return torch.are_deterministic_algorithms_enabled() if flag is None else bool(flag)
+
+
 def _sp2norm_flash_bwd(q, k, v, o, do, row_sums, scale, n_kv_groups=1, window_size=0, use_fast_sqrt=True,
-                       o_lo=None):
+                       o_lo=None, deterministic=None):
     """Run the fused backward; return (dq, dk, dv) like kernels.py:1934-1989.
 
-    o_lo (optional): the forward's residual (``with_residual=True``)."""
+    o_lo (optional): the forward's residual (``with_residual=True``).
+    deterministic: dQ from the query-major kernel, bitwise reproducible
+    (None: follow ``torch.use_deterministic_algorithms``)."""
+    det = _deterministic(deterministic)
     if _tracing(q, k, v, o, do, row_sums):
         lo = o_lo if o_lo is not None else o.new_empty(0)
-        return _ops().flash_bwd(q, k, v, o, lo, do, row_sums, float(scale), int(window_size), bool(use_fast_sqrt))
-    return _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt, o_lo=o_lo)
+        return _ops().flash_bwd(q, k, v, o, lo, do, row_sums, float(scale), int(window_size), bool(use_fast_sqrt),
+                                det)
+    return _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt, o_lo=o_lo,
+                             deterministic=det)
 
 
-def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt, o_lo=None):
+def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqrt, o_lo=None, deterministic=False):
     B, H_q, T, D = q.shape
     H_kv = k.shape[1]
     do = _flash_ready(do)
@@ -580,7 +590,8 @@ def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqr
             B, H_q, H_kv, T, D,
             _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o), _lib.strides(do),
             _lib.strides(dq), _lib.strides(dk), _lib.strides(dv),
-            float(scale), int(window_size), int(not use_fast_sqrt), _DTYPE_CODE[q.dtype], _stream(q),
+            float(scale), int(window_size), int(not use_fast_sqrt), _DTYPE_CODE[q.dtype], int(bool(deterministic)),
+            _stream(q),
         )
     _lib.check(st, "sa_flash_bwd")
     return dq, dk, dv
@@ -588,7 +599,7 @@ def _flash_bwd_direct(q, k, v, o, do, row_sums, scale, window_size, use_fast_sqr
 
 class _SP2NormFlashAttentionFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt):
+    def forward(ctx, q, k, v, scale, n_kv_groups, window_size, use_fast_sqrt, deterministic=None):
         if not _tracing(q, k, v):  # the traced op readies its inputs itself
             q, k, v = _flash_ready(q), _flash_ready(k), _flash_ready(v)
         train = any(ctx.needs_input_grad[:3])
@@ -599,22 +610,27 @@ class _SP2NormFlashAttentionFn(torch.autograd.Function):
         ctx.n_kv_groups = n_kv_groups
         ctx.window_size = window_size
         ctx.use_fast_sqrt = use_fast_sqrt
+        ctx.deterministic = deterministic
         return o
 
     @staticmethod
     def backward(ctx, grad_output):
         q, k, v, o, row_sums, o_lo = ctx.saved_tensors
         dq, dk, dv = _sp2norm_flash_bwd(q, k, v, o, grad_output, row_sums, ctx.scale, ctx.n_kv_groups,
-                                        ctx.window_size, use_fast_sqrt=ctx.use_fast_sqrt, o_lo=o_lo)
-        return dq, dk, dv, None, None, None, None
+                                        ctx.window_size, use_fast_sqrt=ctx.use_fast_sqrt, o_lo=o_lo,
+                                        deterministic=ctx.deterministic)
+        return dq, dk, dv, None, None, None, None, None
 
 
-def sp2norm_flash_attention(q, k, v, *, scale=None, window_size=0, exact_math=False):
+def sp2norm_flash_attention(q, k, v, *, scale=None, window_size=0, exact_math=False, deterministic=None):
     """Fused QK^T -> squareplus norm -> V without materializing the T x T scores.
 
     Supports autograd, GQA/MQA and sliding windows (kernels.py:2016-2050).
     q: [B, H_q, T, D]; k, v: [B, H_kv, T, D] (any strides); bf16 or fp16;
-    D in {32, 64, 128}.
+    D in {32, 64, 128}.  deterministic (an addition to the reference's
+    signature; None follows ``torch.use_deterministic_algorithms``): compute
+    dQ in the query-major kernel with a fixed summation order, so the
+    backward is bitwise reproducible.
     """
     assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
     B, H_q, T, D = q.shape
@@ -624,7 +640,7 @@ def sp2norm_flash_attention(q, k, v, *, scale=None, window_size=0, exact_math=Fa
     _flash_check(q, k, v)
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    return _SP2NormFlashAttentionFn.apply(q, k, v, scale, H_q // H_kv, window_size, not exact_math)
+    return _SP2NormFlashAttentionFn.apply(q, k, v, scale, H_q // H_kv, window_size, not exact_math, deterministic)
 
 
 def sp2norm_flash_attention_chunk(q, k, v, q_offset, *, scale=None, window_size=0, exact_math=False,
@@ -676,7 +692,7 @@ def _flash_fwd_chunk_direct(q, k, v, q_offset, scale, window_size, exact_math, w
 
 
 def sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, row_sums, q_offset, *, scale=None, window_size=0,
-                                      exact_math=False, o_lo=None):
+                                      exact_math=False, o_lo=None, deterministic=None):
     """Backward of ``sp2norm_flash_attention_chunk`` (``sa_flash_bwd_chunk``).
 
     Returns (dq [B, H_q, Tq, D], dk, dv [B, H_kv, Tk, D]): dq is complete for
@@ -687,14 +703,16 @@ def sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, row_sums, q_offset, *, sca
     D = q.shape[3]
     if scale is None:
         scale = 1.0 / math.sqrt(D)
+    det = _deterministic(deterministic)
     if _tracing(q, k, v, o, do, row_sums):
         lo = o_lo if o_lo is not None else o.new_empty(0)
         return _ops().flash_bwd_chunk(q, k, v, o, lo, do, row_sums, int(q_offset), float(scale), int(window_size),
-                                      bool(exact_math))
-    return _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math, o_lo)
+                                      bool(exact_math), det)
+    return _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math, o_lo, det)
 
 
-def _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math, o_lo=None):
+def _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_size, exact_math, o_lo=None,
+                            deterministic=False):
     B, H_q, Tq, D = q.shape
     H_kv, Tk = k.shape[1], k.shape[2]
     q, k, v, o, do = (_flash_ready(t) for t in (q, k, v, o, do))
@@ -714,7 +732,8 @@ def _flash_bwd_chunk_direct(q, k, v, o, do, row_sums, q_offset, scale, window_si
             B, H_q, H_kv, Tq, Tk, int(q_offset), D,
             _lib.strides(q), _lib.strides(k), _lib.strides(v), _lib.strides(o), _lib.strides(do),
             _lib.strides(dq), _lib.strides(dk), _lib.strides(dv),
-            float(scale), int(window_size), int(bool(exact_math)), _DTYPE_CODE[q.dtype], _stream(q),
+            float(scale), int(window_size), int(bool(exact_math)), _DTYPE_CODE[q.dtype], int(bool(deterministic)),
+            _stream(q),
         )
     _lib.check(st, "sa_flash_bwd_chunk")
     return dq, dk, dv

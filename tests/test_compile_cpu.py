@@ -93,7 +93,7 @@ def test_backward_ops_fake_shapes(fake):
     assert o.shape == q.shape and o.is_contiguous() and rs.shape == (1, 8, 96) and rs.dtype == torch.float32
     assert lo.shape == o.shape and lo.dtype == o.dtype
     assert OPS.flash_fwd(q, k, v, 0.1, 0, True, False)[2].numel() == 0
-    dq, dk, dv = OPS.flash_bwd(q, k, v, o, lo, torch.randn_like(o), rs, 0.1, 0, True)
+    dq, dk, dv = OPS.flash_bwd(q, k, v, o, lo, torch.randn_like(o), rs, 0.1, 0, True, False)
     assert (dq.shape, dk.shape, dv.shape) == (q.shape, k.shape, v.shape)
     assert all(t.dtype == torch.float16 and t.is_contiguous() for t in (dq, dk, dv))
     x = _t(3, 50, 50)

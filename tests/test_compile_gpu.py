@@ -92,12 +92,13 @@ def test_opcheck_all_ops():
         (OPS.norm_causal_bwd, (x, randn(x.shape, 8, torch.float32, CUDA), xr, 2.0, 0.5, 2)),
         (OPS.flash_fwd, (q, k, v, 0.125, 0, True, True)),
         (OPS.flash_fwd, (q, k, v, 0.125, 0, True, False)),
-        (OPS.flash_bwd, (q, k, v, o, lo, do, rs, 0.125, 0, True)),
-        (OPS.flash_bwd, (q, k, v, o, o.new_empty(0), do, rs, 0.125, 0, True)),
+        (OPS.flash_bwd, (q, k, v, o, lo, do, rs, 0.125, 0, True, False)),
+        (OPS.flash_bwd, (q, k, v, o, lo, do, rs, 0.125, 0, True, True)),
+        (OPS.flash_bwd, (q, k, v, o, o.new_empty(0), do, rs, 0.125, 0, True, False)),
         (OPS.flash_fwd_chunk, (q[:, :, 64:], k, v, 64, 0.125, 0, False, True)),
         (OPS.flash_bwd_chunk, (q[:, :, 64:].contiguous(), k, v, o[:, :, 64:].contiguous(),
                                lo[:, :, 64:].contiguous(), do[:, :, 64:].contiguous(),
-                               rs[:, :, 64:].contiguous(), 64, 0.125, 0, False)),
+                               rs[:, :, 64:].contiguous(), 64, 0.125, 0, False, True)),
         (OPS.rope_flash_fwd, (q, k, v, cos, sin, 0.125, 0)),
         (OPS.out_proj, (q.view(-1, 64)[:192], randn((64, 40), 11, torch.bfloat16, CUDA))),
         (OPS.fp8_flash_fwd, (q, k, v, 0.125, 0)),

@@ -289,3 +289,59 @@ def test_flash_more_than_65535_heads():
         ref = O.sp2norm_flash_attention(np32(q[sl]), np32(k[sl]), np32(v[sl]))
         assert_close(np32(o[sl]), ref, **FWD_TOL)
         _check_grads((q.grad[sl], k.grad[sl], v.grad[sl]), q[sl], k[sl], v[sl], do[sl])
+
+
+# ---- deterministic dQ (query-major kernel) -----------------------------------
+
+
+def _grads(q, k, v, do, W=0, det=None):
+    q, k, v = (t.detach().requires_grad_(True) for t in (q, k, v))
+    o = sa.sp2norm_flash_attention(q, k, v, window_size=W, deterministic=det)
+    o.backward(do)
+    return q.grad, k.grad, v.grad
+
+
+@pytest.mark.parametrize(("Hq", "Hkv", "T", "D", "W"), [(2, 2, 1, 32, 0), (2, 2, 129, 64, 0), (4, 2, 300, 128, 0),
+                                                        (8, 2, 256, 32, 64), (2, 1, 1024, 128, 0),
+                                                        (2, 2, 333, 128, 100)])
+def test_flash_bwd_deterministic_matches_oracle(Hq, Hkv, T, D, W):
+    q, k, v = _qkv(1, Hq, Hkv, T, D, seed=T + D + Hq)
+    do = randn((1, Hq, T, D), T + 5, torch.bfloat16, CUDA)
+    got = _grads(q, k, v, do, W, det=True)
+    _check_grads(got, q, k, v, do, window=W)
+    # dK / dV come from the same key-major kernel either way: bitwise equal
+    ref = _grads(q, k, v, do, W, det=False)
+    assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2])
+
+
+def test_flash_bwd_deterministic_is_bitwise_repeatable():
+    q, k, v = _qkv(2, 8, 4, 4096, 128, seed=7)
+    do = randn((2, 8, 4096, 128), 8, torch.bfloat16, CUDA)
+    a = _grads(q, k, v, do, det=True)
+    b = _grads(q, k, v, do, det=True)
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    # torch.use_deterministic_algorithms selects the same path by default
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    try:
+        c = _grads(q, k, v, do)
+    finally:
+        torch.use_deterministic_algorithms(prev)
+    assert torch.equal(a[0], c[0])
+
+
+def test_flash_bwd_chunk_deterministic():
+    from smooth_attn.kernels import sp2norm_flash_attention_chunk_bwd
+
+    Tq, Tk, off = 200, 700, 500
+    q = randn((1, 4, Tq, 128), 1, torch.bfloat16, CUDA)
+    k = randn((1, 2, Tk, 128), 2, torch.bfloat16, CUDA)
+    v = randn((1, 2, Tk, 128), 3, torch.bfloat16, CUDA)
+    do = randn((1, 4, Tq, 128), 4, torch.bfloat16, CUDA)
+    o, rs, lo = sa.sp2norm_flash_attention_chunk(q, k, v, off, window_size=96, return_residual=True)
+    got = sp2norm_flash_attention_chunk_bwd(q, k, v, o, do, rs, off, window_size=96, o_lo=lo, deterministic=True)
+    args = (np32(q), np32(k), np32(v), np32(do), off)
+    ref = O.chunk_flash_attention_bwd(*args, window_size=96, acc=np.float64)
+    emu = O.chunk_flash_attention_bwd(*args, window_size=96, emulate=True)
+    for g, r, m in zip(got, ref, emu):
+        check_bf16_grads(np32(g), r, m, **BWD_TOL)
