@@ -163,13 +163,12 @@ SA_API int64_t sa_flash_bwd_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, i
  * sa_flash_bwd_workspace_size() bytes, 256 B aligned, contents undefined on
  * entry.  sa_flash_bwd_workspace_size() returns 0 for sizes whose byte
  * count overflows int64; such problems are rejected.
- * D = 128 (and any D with deterministic != 0): the key-major kernel computes
- * dK and dV only and a query-major kernel sums each dQ row over the key tiles
- * in a fixed order inside one CTA (the reference's order,
- * kernels.py:1680-1784): bitwise reproducible.  D = 32 / 64 with
  * deterministic = 0: dQ is accumulated by the key-major kernel with fp32
- * atomics (the order of the adds, and so dQ's last bits, varies from run to
- * run) and S and dP are computed once instead of twice.
+ * atomics (fastest; the order of the adds, and so dQ's last bits, varies
+ * from run to run).  deterministic != 0: the key-major kernel computes dK and
+ * dV only and a query-major kernel sums each dQ row over the key tiles in a
+ * fixed order inside one CTA (the reference's order, kernels.py:1680-1784):
+ * bitwise reproducible, at the cost of recomputing S and dP once more.
  *
  * Replaces: _sp2norm_flash_bwd, _sp2norm_flash_bwd_dq_kernel,
  *           _sp2norm_flash_bwd_dkv_kernel

@@ -57,6 +57,15 @@ __device__ __forceinline__ bool b_wait(uint64_t* bar, uint32_t phase, bool& fail
   return true;
 }
 
+__device__ __forceinline__ bool b_warp_wait_spin(uint64_t* bar, uint32_t phase, bool& failed) {
+  const bool ok = __all_sync(0xffffffffu, !failed && mbar_wait_spin(bar, phase));
+  if (!ok) {
+    if (!failed && (threadIdx.x & 31) == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
+    failed = true;
+  }
+  return ok;
+}
+
 __device__ __forceinline__ bool b_warp_wait(uint64_t* bar, uint32_t phase, bool& failed) {
   const bool ok = __all_sync(0xffffffffu, !failed && mbar_wait(bar, phase));
   if (!ok) {
@@ -435,32 +444,472 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------
-// D = 128 backward, dK and dV: one CTA per 128-row KV tile of one (b, kv head),
+// D = 128 backward: 64-row query tiles, double-buffered S^T / dP^T in TMEM.
+//
+// TMEM (512 columns): S^T_b @ 64b and dP^T_b @ 128 + 64b (both double-
+// buffered), dK @ 256, dV @ 384.  dQ is produced transposed, dQ^T = K^T dS^T
+// (M = the 128 head-dim rows, N = 64 query columns), into the dP^T buffer of
+// its own tile after the elementwise stage consumed it, so everything fits.
+// S^T and dP^T of tile i+2 are issued while tile i+1's elementwise stage runs.
+// Warps: 0-7 elementwise (two warpgroups, 32 query columns each), 8-11 dQ
+// drain (TMEM lane = head-dim index: coalesced fp32 atomics), 12 TMA, 13 MMA.
+// ---------------------------------------------------------------------------
+struct Bwd128 {
+  static constexpr int D = 128, BN = 128, BQ = 64, NS = 3;
+  static constexpr int KV_TILE = 128 * D * 2;  // 2 chunks of 128 rows x 128 B
+  static constexpr int Q_TILE = BQ * D * 2;    // 2 chunks of 64 rows x 128 B
+  static constexpr int DS_TILE = BN * BQ * 2;  // [128 kv][64 q], 128 B swizzle
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + KV_TILE;
+  static constexpr int OFF_Q = OFF_V + KV_TILE;
+  static constexpr int OFF_DO = OFF_Q + NS * Q_TILE;
+  static constexpr int OFF_DS = OFF_DO + NS * Q_TILE;
+  static constexpr int OFF_VEC = OFF_DS + 2 * DS_TILE;  // [2 buffers][3][64] per-column constants
+  static constexpr int OFF_BAR = OFF_VEC + 2 * 3 * 64 * 4;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int THREADS = 448;
+};
+
+struct Bwd128Bars {
+  uint64_t kv_full;
+  uint64_t q_full[3], q_empty[3];
+  uint64_t s_full[2];   // S^T of tile j ready in buffer j&1
+  uint64_t dp_full[2];  // dP^T of tile j ready in buffer j&1
+  uint64_t p_ready;    // elementwise stage of tile j done (256 arrivals)
+  // dK(j), dQ^T(j) complete, in barrier j&1.  The drain releases dq_free
+  // before its atomics, so the MMA can finish tile j+2 before the drain waits
+  // for tile j+1; one barrier per tile parity keeps each barrier at most one
+  // phase ahead of its waiter (a single barrier could complete twice).
+  uint64_t mm2_done[2];
+  uint64_t dq_free;    // dQ^T(j) read out of TMEM (128 arrivals): dP^T buffer j&1 free
+  uint64_t all_done;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void ew_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+
+// AND of `v` over the 256 elementwise threads (also a barrier among them).
+__device__ __forceinline__ bool ew_all(bool v) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 2, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)v)
+      : "memory");
+  return out != 0;
+}
+
+// Per query column m the loader stores c4[m] = 1/(4R), cs[m] = scale/R and
+// -cd[m] = -delta*scale/R, so with t = a + sqrt(a^2+4) = 2 sp and
+// h = 1 + a rsqrt(a^2+4) = 2 sp':
+//   P  = sp^2 / R                      = t*t*c4
+//   dS = (dP - delta)/R * 4 sp sp' s   = (dP*cs - cd) * t*h = (dP*cs - cd) * t*t*rsqrt(a^2+4)
+// Both 32-column TMEM loads are issued together (one latency); results are
+// packed and stored 16 columns at a time to keep register use low.
+template <bool BF16, bool EXACT, bool MASK>
+__device__ __forceinline__ void bwd128_chunk(uint32_t tS, uint32_t tP, int w2, uint8_t* dsrow, int r,
+                                             const float* vec, float scale2, int n, int q0, int qend, int Tk,
+                                             int window) {
+  uint32_t sv[32], dv[32];
+  tmem_ld32(tS + 32 * w2, sv);
+  tmem_ld32(tP + 32 * w2, dv);
+  tmem_ld_wait(sv);
+  tmem_ld_wait(dv);
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    const int col = 32 * w2 + 16 * hf;
+    uint32_t pk[8], dk[8];
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      const float4 c4v = *reinterpret_cast<const float4*>(vec + col + e);
+      const float4 csv = *reinterpret_cast<const float4*>(vec + 64 + col + e);
+      const float4 cdv = *reinterpret_cast<const float4*>(vec + 128 + col + e);  // -cd
+      const float2 c4p[2] = {make_float2(c4v.x, c4v.y), make_float2(c4v.z, c4v.w)};
+      const float2 csp[2] = {make_float2(csv.x, csv.y), make_float2(csv.z, csv.w)};
+      const float2 cdp[2] = {make_float2(cdv.x, cdv.y), make_float2(cdv.z, cdv.w)};
+      float pv[4], dsv[4];
+      // two query columns per packed fp32x2 instruction (bit-identical to the
+      // scalar ops; the elementwise stage bounds this kernel's issue slots)
+#pragma unroll
+      for (int u = 0; u < 4; u += 2) {
+        const int idx = 16 * hf + e + u;
+        const float2 a = ffma2(make_float2(__uint_as_float(sv[idx]), __uint_as_float(sv[idx + 1])),
+                               make_float2(scale2, scale2), make_float2(-1.0f, -1.0f));
+        const float2 w = ffma2(a, a, make_float2(4.0f, 4.0f));
+        const float2 rs = make_float2(rsqrt_approx(w.x), rsqrt_approx(w.y));
+        const float2 t = EXACT ? make_float2(a.x + sqrtf(w.x), a.y + sqrtf(w.y)) : ffma2(w, rs, a);
+        // 4 sp sp' = t (1 + a rsqrt(w)) = t^2 rsqrt(w): one multiply fewer, and
+        // no cancellation in 1 + a rsqrt(w) for very negative a
+        const float2 tt = fmul2(t, t);
+        float2 pp = fmul2(tt, c4p[u / 2]);
+        float2 ds = fmul2(ffma2(make_float2(__uint_as_float(dv[idx]), __uint_as_float(dv[idx + 1])), csp[u / 2],
+                                cdp[u / 2]),
+                          fmul2(tt, rs));
+        if (MASK) {
+          const int q = q0 + col + e + u;  // global query position
+          const bool ok0 = (n <= q) && (q < qend) && (n < Tk) && (window <= 0 || q - n < window);
+          const bool ok1 = (n <= q + 1) && (q + 1 < qend) && (n < Tk) && (window <= 0 || q + 1 - n < window);
+          pp.x = ok0 ? pp.x : 0.f;
+          ds.x = ok0 ? ds.x : 0.f;
+          pp.y = ok1 ? pp.y : 0.f;
+          ds.y = ok1 ? ds.y : 0.f;
+        }
+        pv[u] = pp.x;
+        pv[u + 1] = pp.y;
+        dsv[u] = ds.x;
+        dsv[u + 1] = ds.y;
+      }
+      pk[e / 2] = BF16 ? pack2_bf16(pv[0], pv[1]) : pack2_f16(pv[0], pv[1]);
+      pk[e / 2 + 1] = BF16 ? pack2_bf16(pv[2], pv[3]) : pack2_f16(pv[2], pv[3]);
+      dk[e / 2] = BF16 ? pack2_bf16(dsv[0], dsv[1]) : pack2_f16(dsv[0], dsv[1]);
+      dk[e / 2 + 1] = BF16 ? pack2_bf16(dsv[2], dsv[3]) : pack2_f16(dsv[2], dsv[3]);
+    }
+    // P of query columns [32 w2, 32 w2 + 32) goes over this warpgroup's own,
+    // already-read S^T columns [32 w2, 32 w2 + 16): no cross-warpgroup hazard.
+    tmem_st8(tS + 32 * w2 + 8 * hf, pk);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int piece = (w2 * 4 + hf * 2 + j) ^ (r & 7);
+      *reinterpret_cast<uint4*>(dsrow + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+    }
+  }
+}
+
+template <bool BF16, bool EXACT>
+__global__ void __launch_bounds__(448, 1)
+    sp2_bwd128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
+                        BwdParams p) {
+  using C = Bwd128;
+  constexpr int D = C::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sQ = smem + C::OFF_Q;
+  uint8_t* sDO = smem + C::OFF_DO;
+  uint8_t* sDS = smem + C::OFF_DS;
+  float* vVec = reinterpret_cast<float*>(smem + C::OFF_VEC);  // [2][3][64]
+  Bwd128Bars* bars = reinterpret_cast<Bwd128Bars*>(smem + C::OFF_BAR);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int kvt, bhk;  // KV tile (0 = most query tiles) and (batch, kv head)
+  // one head at a time (group of 1): measured faster here than the grouped
+  // order the forward uses, which lengthened this kernel's step
+  grouped_longest_first((int)blockIdx.x, (p.Tk + C::BN - 1) / C::BN, p.B * p.Hkv, 1, kvt, bhk);
+  const int n0 = kvt * C::BN;
+  const int b = bhk / p.Hkv, kvh = bhk % p.Hkv;
+  const int G = p.Hq / p.Hkv;
+  int qt_first, qt_last;
+  query_tile_range(p, n0, C::BN, C::BQ, qt_first, qt_last);
+  const int per_head = qt_last - qt_first + 1;
+  const int ntiles = per_head > 0 ? G * per_head : 0;
+  if (ntiles == 0) {  // no query sees these keys: dK = dV = 0 (before any barrier)
+    zero_dkdv<D, C::BN>(p, b, kvh, n0);
+    return;
+  }
+  // Tiles run head-major: (head kvh*G + g, query tile qt_first .. qt_last).
+  // Each role walks them with an incremental cursor (no integer division).
+  struct Cursor {
+    int h, qt;
+  };
+  auto advance = [&](Cursor& c) {
+    if (++c.qt > qt_last) {
+      c.qt = qt_first;
+      ++c.h;
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars->q_full[i], 1);
+      mbar_init(&bars->q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->s_full[i], 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->dp_full[i], 1);
+    mbar_init(&bars->p_ready, 256);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->mm2_done[i], 1);
+    mbar_init(&bars->dq_free, 128);
+    mbar_init(&bars->all_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 13) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  bool failed = false;
+
+  if (warp == 12) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      tma_prefetch_desc(&tmdo);
+      mbar_arrive_expect_tx(&bars->kv_full, 2 * C::KV_TILE);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_4d(sK + c * 128 * 128, &tmk, c * 64, n0, kvh, b, &bars->kv_full);
+        tma_load_4d(sV + c * 128 * 128, &tmv, c * 64, n0, kvh, b, &bars->kv_full);
+      }
+      Cursor cur{kvh * G, qt_first};
+      for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
+        const int st = it % C::NS;
+        if (it >= C::NS && !b_wait(&bars->q_empty[st], ((it / C::NS) - 1) & 1, failed)) break;
+        const int h = cur.h;
+        const int q0 = cur.qt * C::BQ;
+        mbar_arrive_expect_tx(&bars->q_full[st], 2 * C::Q_TILE);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_4d(sQ + st * C::Q_TILE + c * C::BQ * 128, &tmq, c * 64, q0, h, b, &bars->q_full[st]);
+          tma_load_4d(sDO + st * C::Q_TILE + c * C::BQ * 128, &tmdo, c * 64, q0, h, b, &bars->q_full[st]);
+        }
+      }
+    }
+  } else if (warp == 13) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr int ab = BF16 ? 1 : 0;
+      constexpr uint32_t id_s = idesc_f16(128, C::BQ, ab, 0, 0);  // S^T, dP^T
+      constexpr uint32_t id_kv = idesc_f16(128, D, ab, 0, 1);     // dV, dK: B (dO / Q) MN-major
+      constexpr uint32_t id_dq = idesc_f16(128, C::BQ, ab, 1, 1); // dQ^T: A = K^T MN-major, B = dS^T MN-major
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
+      const uint32_t aDS = smem_u32(sDS);
+      const uint32_t tDK = tbase + 256, tDV = tbase + 384;
+      // descriptors are built once and advanced with plain adds in the MMA loops
+      const uint64_t dK0 = smem_desc(aK, 16, 1024, SW_128B), dV0 = smem_desc(aV, 16, 1024, SW_128B);
+      const uint64_t dKt0 = smem_desc(aK, 128 * 128, 1024, SW_128B);  // K as MN-major A (K^T)
+      auto issue_s = [&](int it) {  // S^T(it) = K Q^T -> buffer it&1
+        const uint64_t dq0 = smem_desc(aQ + (it % C::NS) * C::Q_TILE, 16, 1024, SW_128B);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;  // K: 128-row chunks
+          const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;  // Q: 64-row chunks
+          mma_ss(tbase + (it & 1) * 64, desc_add(dK0, koff), desc_add(dq0, qoff), id_s, kk > 0);
+        }
+        mma_commit(&bars->s_full[it & 1]);
+      };
+      auto issue_dp = [&](int it) {  // dP^T(it) = V dO^T -> dP^T buffer it&1
+        const uint64_t ddo0 = smem_desc(aDO + (it % C::NS) * C::Q_TILE, 16, 1024, SW_128B);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t koff = (kk / 4) * 128 * 128 + (kk % 4) * 32;
+          const uint32_t qoff = (kk / 4) * C::BQ * 128 + (kk % 4) * 32;
+          mma_ss(tbase + 128 + (it & 1) * 64, desc_add(dV0, koff), desc_add(ddo0, qoff), id_s, kk > 0);
+        }
+        mma_commit(&bars->dp_full[it & 1]);
+      };
+      // Per tile j, once its elementwise stage is done: dV(j), dK(j), dQ^T(j)
+      // into the dP^T buffer elementwise(j) consumed, then for tile j+2: S^T
+      // (in issue order after dV(j), which reads P(j) from the same columns)
+      // and, once dQ^T(j) is drained, dP^T.  S^T and dP^T of tile j+1 were
+      // issued a tile earlier, so elementwise(j+1) starts without waiting.
+      if (b_wait(&bars->kv_full, 0, failed) && ntiles > 0 && b_wait(&bars->q_full[0], 0, failed)) {
+        tc_fence_after();
+        issue_s(0);
+        issue_dp(0);
+        if (ntiles > 1 && b_wait(&bars->q_full[1], 0, failed)) {
+          tc_fence_after();
+          issue_s(1);
+          issue_dp(1);
+        }
+        for (int it = 0; it < ntiles && !failed; ++it) {
+          const int bb = it & 1, st = it % C::NS;
+          if (!b_wait(&bars->p_ready, it & 1, failed)) break;
+          tc_fence_after();
+          const uint32_t q_s = aQ + st * C::Q_TILE, do_s = aDO + st * C::Q_TILE;
+          const uint32_t ds_s = aDS + bb * C::DS_TILE;
+          const uint64_t bdo0 = smem_desc(do_s, C::BQ * 128, 1024, SW_128B);
+          const uint64_t bq0 = smem_desc(q_s, C::BQ * 128, 1024, SW_128B);
+          const uint64_t ads0 = smem_desc(ds_s, 16, 1024, SW_128B);
+          const uint64_t bds0 = smem_desc(ds_s, C::DS_TILE, 1024, SW_128B);
+#pragma unroll
+          for (int kk = 0; kk < C::BQ / 16; ++kk) {  // dV += P^T dO, K = 64 query rows
+            const uint64_t b_do = desc_add(bdo0, kk * 16 * 128);
+            // P of query rows [16 kk, 16 kk + 16) sits at columns 32 (kk / 2) + 8 (kk % 2)
+            mma_ts(tDV, tbase + bb * 64 + (kk >> 1) * 32 + (kk & 1) * 8, b_do, id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < C::BQ / 16; ++kk) {  // dK += dS^T Q
+            mma_ss(tDK, desc_add(ads0, kk * 32), desc_add(bq0, kk * 16 * 128), id_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk) {  // dQ^T = K^T dS^T into dP^T buffer bb (consumed)
+            mma_ss(tbase + 128 + bb * 64, desc_add(dKt0, kk * 16 * 128), desc_add(bds0, kk * 16 * 128), id_dq, kk > 0);
+          }
+          mma_commit(&bars->mm2_done[bb]);
+          mma_commit(&bars->q_empty[st]);
+          if (it + 2 < ntiles) {
+            const int nx = it + 2;
+            if (!b_wait(&bars->q_full[nx % C::NS], (nx / C::NS) & 1, failed)) break;
+            tc_fence_after();
+            // S^T(nx) overwrites the columns dV(it) reads P from: tcgen05.mma
+            // ops of one thread execute in issue order, so no wait is needed.
+            issue_s(nx);
+            if (!b_wait(&bars->dq_free, it & 1, failed)) break;
+            tc_fence_after();
+            issue_dp(nx);
+          }
+        }
+      }
+      mma_commit(&bars->all_done);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ dQ drain
+    const int g = warp & 3;
+    const int d = 32 * g + lane;  // TMEM lane = head-dim index of dQ^T
+    const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
+    Cursor cur{kvh * G, qt_first};
+    for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
+      // polling (not suspending): the drain's reaction time gates the next dP^T
+      if (!b_warp_wait_spin(&bars->mm2_done[it & 1], (it >> 1) & 1, failed)) break;
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tl + 128 + (it & 1) * 64, v0);  // dQ^T(it) sits in dP^T buffer it&1
+      tmem_ld32(tl + 128 + (it & 1) * 64 + 32, v1);
+      tmem_ld_wait(v0);
+      tmem_ld_wait(v1);
+      tc_fence_before();
+      mbar_arrive(&bars->dq_free);
+      const int h = cur.h;
+      const int q0 = cur.qt * C::BQ;
+      float* dst = p.dq_acc + (((int64_t)b * p.Hq + h) * p.T + q0) * D + d;
+      const int lim = p.T - q0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < lim) atomicAdd(dst + (int64_t)j * D, __uint_as_float(v0[j]));
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (32 + j < lim) atomicAdd(dst + (int64_t)(32 + j) * D, __uint_as_float(v1[j]));
+    }
+  } else {
+    // ------------------------------------------------------------ elementwise warpgroups
+    const int w2 = warp >> 2;  // query-column half
+    const int g = warp & 3;
+    const int r = 32 * g + lane;  // TMEM lane = KV row
+    const int n = n0 + r;
+    const int tid = threadIdx.x;  // 0..255
+    const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
+    const float scale2 = 2.0f * p.scale;
+    // R and delta of the next tile's query column `tid` (threads 0..63) are
+    // loaded a tile ahead into registers.  The loads are unconditional (from a
+    // valid index) and the validity flag is applied when the values are used,
+    // so nothing waits on the load before the tile's barrier.
+    float pre_r = 0.f, pre_d = 0.f;
+    bool pre_ok = false;
+    Cursor nxt{kvh * G, qt_first};  // tile the next prefetch loads
+    auto prefetch = [&](int it) {  // threads 0..63: R and delta of query column tid
+      const Cursor c = nxt;
+      advance(nxt);
+      if (tid >= 64) return;
+      const int h = it < ntiles ? c.h : kvh * G;
+      const int qq = c.qt * C::BQ + tid;
+      pre_ok = it < ntiles && qq < p.T;
+      const int64_t idx = ((int64_t)b * p.Hq + h) * p.T + (qq < p.T ? qq : 0);
+      pre_r = __ldg(p.rowsum + idx);
+      pre_d = __ldg(p.delta + idx);
+    };
+    prefetch(0);
+    Cursor cur{kvh * G, qt_first};
+    for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
+      const int bb = it & 1;
+      const int q0 = cur.qt * C::BQ;
+      // buffer bb was last read in tile it-2; every thread finished that
+      // before the barrier below of tile it-1, so no barrier is needed here
+      if (tid < 64) {
+        const float ir = pre_ok ? 1.0f / pre_r : 0.f;
+        float* vb = vVec + bb * 192;
+        vb[tid] = 0.25f * ir;
+        vb[64 + tid] = p.scale * ir;
+        vb[128 + tid] = -(pre_d * p.scale * ir);  // stored negated: dP*cs - cd is one fma
+      }
+      ew_sync();
+      prefetch(it + 1);
+      // all 256 threads leave together on a timeout (the chunk below has a named barrier)
+      if (!ew_all(mbar_wait(&bars->s_full[bb], (it >> 1) & 1) && mbar_wait(&bars->dp_full[bb], (it >> 1) & 1))) {
+        if (tid == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const int q0g = q0 + p.qoff, qend = p.qoff + p.T;  // global query positions
+      const bool need_mask = (q0g < n0 + C::BN - 1) || (q0 + C::BQ > p.T) || (n0 + C::BN > p.Tk) ||
+                             (p.window > 0 && q0g + C::BQ - 1 - n0 >= p.window);
+      uint8_t* dsrow = sDS + bb * C::DS_TILE + r * 128;
+      if (need_mask)
+        bwd128_chunk<BF16, EXACT, true>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vVec + bb * 192, scale2,
+                                        n, q0g, qend, p.Tk, p.window);
+      else
+        bwd128_chunk<BF16, EXACT, false>(tl + bb * 64, tl + 128 + bb * 64, w2, dsrow, r, vVec + bb * 192, scale2,
+                                         n, q0g, qend, p.Tk, p.window);
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->p_ready);
+    }
+    // epilogue: warpgroup 0 writes dK, warpgroup 1 writes dV (TMEM lane = KV row)
+    if (b_warp_wait(&bars->all_done, 0, failed)) {
+      tc_fence_after();
+      const bool live = n < p.Tk;
+      uint8_t* base = static_cast<uint8_t*>(w2 ? p.dv : p.dk) +
+                      2 * (w2 ? ((int64_t)b * p.sdv_b + (int64_t)kvh * p.sdv_h + (int64_t)n * p.sdv_s)
+                              : ((int64_t)b * p.sdk_b + (int64_t)kvh * p.sdk_h + (int64_t)n * p.sdk_s));
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tl + 256 + w2 * 128 + c * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          pk[e / 2] = BF16 ? pack2_bf16(__uint_as_float(v[e]), __uint_as_float(v[e + 1]))
+                           : pack2_f16(__uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+        if (live) {
+          uint4* dst = reinterpret_cast<uint4*>(base + c * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 13) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// D = 128 backward, dK and dV only (the deterministic path): one CTA per 128-row KV tile of one (b, kv head),
 // 128-row query tiles, so every tcgen05.mma is 128 x 128 x 16 (an N = 64 MMA
 // takes 48 tensor cycles for half the work of a 64-cycle N = 128 one).  K and
 // V stay in shared memory; Q / dO stream through two stages.  dQ comes from
-// the query-major kernel below (sp2_bwd_dq_kernel): summing dQ here would
-// take fp32 atomics of every (query tile, KV tile) partial, and their traffic,
-// not the tensor pipe, bounded the kernels that did it.
+// the query-major kernel below (sp2_bwd_dq_kernel), which sums it in a fixed
+// order.  (Summing dQ here, with 128-row query tiles, took fp32 atomics of
+// twice the partials per CTA and ran slower than the 64-row kernel above.)
 //
-// TMEM (512 columns): S^T @0, dP^T @128 (dS^T is written over it), dK @256,
+// TMEM (512 columns): S^T @0 (P is written over it), dP^T @128, dK @256,
 // dV @384.  With S^T and dP^T single-buffered, the elementwise stage runs in
 // two halves so that it overlaps the MMAs:
-//   P half  (needs S^T(i)):  P = sp^2 / R -> shared memory (16-bit, the K-major
-//                            A of dV); g = 4 sp sp' = t^2 rsqrt(a^2 + 4) stays
-//                            in registers
-//   dS half (needs dP^T(i)): dS = (dP scale/R - delta scale/R) g -> TMEM
-//                            (16-bit, over dP^T: the A of dK)
-// S^T's columns are free as soon as the P half has read them, so S^T(i+1)
-// follows the P half of tile i directly.  Tensor-pipe order per tile:
-// S^T(i+1) = K Q^T, dV(i) += P^T dO, dK(i) += dS^T Q, dP^T(i+1) = V dO^T.  The
-// P half of tile i+1 runs under dV(i) .. dP^T(i+1) (it waits for dV(i) only
-// before it stores P), the dS half of tile i under S^T(i+1) and dV(i).
+//   P half  (needs S^T(i)):  P = sp^2 / R -> TMEM (16-bit, over S^T);
+//                            g = 4 sp sp' = t^2 rsqrt(a^2 + 4) stays in registers
+//   dS half (needs dP^T(i)): dS = (dP scale/R - delta scale/R) g -> shared memory
+// Tensor-pipe order per tile: dV(i) += P^T dO, S^T(i+1) = K Q^T,
+// dK(i) += dS^T Q, dP^T(i+1) = V dO^T.  The P half of tile i+1 runs under
+// dK(i) and dP^T(i+1), the dS half of tile i under dV(i) and S^T(i+1).
 // Warps: 0-15 elementwise (four warpgroups of 32 query columns; thread = KV
 // row: four warps per scheduler hide the TMEM-load and MUFU latencies),
 // 16 TMA, 17 MMA.
 // ---------------------------------------------------------------------------
-struct Bwd128 {
+struct DkvCfg {
   static constexpr int D = 128, BN = 128, BQ = 128, NS = 2;
   static constexpr int TILE = 128 * D * 2;     // 32 KB: two 64-column chunks of 128 rows x 128 B
   static constexpr int CH = 128 * 128;         // one chunk
@@ -469,8 +918,8 @@ struct Bwd128 {
   static constexpr int OFF_V = OFF_K + TILE;
   static constexpr int OFF_Q = OFF_V + TILE;
   static constexpr int OFF_DO = OFF_Q + NS * TILE;
-  static constexpr int OFF_P = OFF_DO + NS * TILE;  // P [kv 128][q 128] as two 64-query chunks
-  static constexpr int OFF_VEC = OFF_P + TILE;
+  static constexpr int OFF_DS = OFF_DO + NS * TILE;  // dS [kv 128][q 128] as two 64-query chunks
+  static constexpr int OFF_VEC = OFF_DS + TILE;
   static constexpr int OFF_BAR = OFF_VEC + NS * VEC_TILE;
   // no alignment slack: the kernel checks that dynamic shared memory starts
   // on a 1024-byte boundary (it does when the kernel has no static shared data)
@@ -480,28 +929,29 @@ struct Bwd128 {
   static_assert(SMEM <= 227 * 1024, "shared memory plan");
 };
 
-struct Bwd128Bars {
+struct DkvBars {
   uint64_t kv_full;
   uint64_t q_full[2], q_empty[2];
   uint64_t s_full;    // S^T(i) in TMEM
   uint64_t dp_full;   // dP^T(i) in TMEM (and every earlier MMA done)
-  uint64_t p_ready;   // P(i) in shared memory and S^T(i) read (512 arrivals)
-  uint64_t dv_done;   // dV(i) done: the P tile is free
-  uint64_t ds_ready;  // dS(i) in TMEM over dP^T(i) (512 arrivals)
+  uint64_t p_ready;   // P(i) in TMEM (512 arrivals)
+  uint64_t ds_ready;  // dS(i) in shared memory and dP^T(i) read (512 arrivals)
   uint64_t all_done;
   uint32_t tmem_base;
 };
-static_assert(sizeof(Bwd128Bars) <= 128, "barrier block");
+static_assert(sizeof(DkvBars) <= 128, "barrier block");
 
-// P half for the 32 query columns [32 w4, 32 w4 + 32) of KV row `n`: P
-// (16-bit pairs) and g are returned in registers.  ir[m] = 1/R of query
-// column m; the products round as P = t*t*(ir/4) and g = t*t*rsqrt(a^2+4).
+// P half for the 32 query columns [32 w4, 32 w4 + 32) of KV row `n`.  P
+// (16-bit) goes over the first 16 of these 32 S^T columns; g is returned.
+// ir[m] = 1/R of query column m; the products round as P = t*t*(ir/4) and
+// g = t*t*rsqrt(a^2+4).
 template <bool BF16, bool EXACT, bool MASK>
-__device__ __forceinline__ void bwd128_p(uint32_t tS, int w4, const float* ir, float scale2, float (&g)[32],
-                                         uint32_t (&pk)[16], int n, int q0, int qend, int Tk, int window) {
+__device__ __forceinline__ void dkv_p(uint32_t tS, int w4, const float* ir, float scale2, float (&g)[32],
+                                         int n, int q0, int qend, int Tk, int window) {
   uint32_t sv[32];
   tmem_ld32(tS + 32 * w4, sv);
   tmem_ld_wait(sv);
+  uint32_t pk[16];
 #pragma unroll
   for (int e = 0; e < 32; e += 4) {
     const int col = 32 * w4 + e;
@@ -531,24 +981,17 @@ __device__ __forceinline__ void bwd128_p(uint32_t tS, int w4, const float* ir, f
       pk[(e + u) / 2] = BF16 ? pack2_bf16(pp.x, pp.y) : pack2_f16(pp.x, pp.y);
     }
   }
-}
-
-// 32 query columns (64 bytes) of 16-bit values into row r of a 128-byte-
-// swizzled tile chunk of 64 query columns (row: the chunk's row r); the
-// columns are the 64-byte half w4 & 1 of that row.
-__device__ __forceinline__ void bwd128_store_row(uint8_t* row, int w4, int r, const uint32_t (&pk)[16]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int piece = (4 * (w4 & 1) + j) ^ (r & 7);
-    *reinterpret_cast<uint4*>(row + piece * 16) = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-  }
+  tmem_st8(tS + 32 * w4, *reinterpret_cast<const uint32_t(*)[8]>(&pk[0]));
+  tmem_st8(tS + 32 * w4 + 8, *reinterpret_cast<const uint32_t(*)[8]>(&pk[8]));
 }
 
 // dS half: dS = (dP * scale/R - delta scale/R) * g for the same 32 columns,
-// 16-bit, over the first 16 of these 32 dP^T columns (already read).
+// 16-bit, into row r of the 128-byte-swizzled dS chunk of 64 query columns
+// (dsrow); these columns are the 64-byte half w4 & 1 of that row.
 template <bool BF16, bool MASK>
-__device__ __forceinline__ void bwd128_ds(uint32_t tP, int w4, const float* ir, const float* ncd, float scale,
-                                          const float (&g)[32], int n, int q0, int qend, int Tk, int window) {
+__device__ __forceinline__ void dkv_ds(uint32_t tP, int w4, uint8_t* dsrow, int r, const float* ir,
+                                          const float* ncd, float scale, const float (&g)[32], int n, int q0,
+                                          int qend, int Tk, int window) {
   uint32_t dv[32];
   tmem_ld32(tP + 32 * w4, dv);
   tmem_ld_wait(dv);
@@ -576,16 +1019,19 @@ __device__ __forceinline__ void bwd128_ds(uint32_t tP, int w4, const float* ir, 
       dk[(e + u) / 2] = BF16 ? pack2_bf16(ds.x, ds.y) : pack2_f16(ds.x, ds.y);
     }
   }
-  tmem_st8(tP + 32 * w4, *reinterpret_cast<const uint32_t(*)[8]>(&dk[0]));
-  tmem_st8(tP + 32 * w4 + 8, *reinterpret_cast<const uint32_t(*)[8]>(&dk[8]));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int piece = (4 * (w4 & 1) + j) ^ (r & 7);
+    *reinterpret_cast<uint4*>(dsrow + piece * 16) = make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+  }
 }
 
 template <bool BF16, bool EXACT>
-__global__ void __launch_bounds__(Bwd128::THREADS, 1)
-    sp2_bwd128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+__global__ void __launch_bounds__(DkvCfg::THREADS, 1)
+    sp2_bwd_dkv128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmdo,
                       BwdParams p) {
-  using C = Bwd128;
+  using C = DkvCfg;
   constexpr int D = C::D;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if ((smem_u32(smem_raw) & 1023u) != 0) {  // never expected; all threads leave before any barrier
@@ -597,9 +1043,9 @@ __global__ void __launch_bounds__(Bwd128::THREADS, 1)
   uint8_t* sV = smem + C::OFF_V;
   uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sDO = smem + C::OFF_DO;
-  uint8_t* sP = smem + C::OFF_P;
+  uint8_t* sDS = smem + C::OFF_DS;
   float* vVec = reinterpret_cast<float*>(smem + C::OFF_VEC);  // [NS][2][128]
-  Bwd128Bars* bars = reinterpret_cast<Bwd128Bars*>(smem + C::OFF_BAR);
+  DkvBars* bars = reinterpret_cast<DkvBars*>(smem + C::OFF_BAR);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int kvt, bhk;  // KV tile (0 = most query tiles) and (batch, kv head)
@@ -636,7 +1082,6 @@ __global__ void __launch_bounds__(Bwd128::THREADS, 1)
     mbar_init(&bars->s_full, 1);
     mbar_init(&bars->dp_full, 1);
     mbar_init(&bars->p_ready, C::EW);
-    mbar_init(&bars->dv_done, 1);
     mbar_init(&bars->ds_ready, C::EW);
     mbar_init(&bars->all_done, 1);
     fence_mbar_init();
@@ -687,7 +1132,7 @@ __global__ void __launch_bounds__(Bwd128::THREADS, 1)
       constexpr uint32_t id_kv = idesc_f16(128, D, ab, 0, 1);   // dV, dK: B (dO / Q) MN-major
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
       const uint64_t dK0 = smem_desc(aK, 16, 1024, SW_128B), dV0 = smem_desc(aV, 16, 1024, SW_128B);
-      const uint64_t dPk0 = smem_desc(smem_u32(sP), 16, 1024, SW_128B);  // P^T as a K-major A (dV)
+      const uint64_t dSk0 = smem_desc(smem_u32(sDS), 16, 1024, SW_128B);  // dS^T as a K-major A (dK)
       // K-major operands: 16-element k-steps, 64-element chunks CH bytes apart
       auto koff = [](int kk) { return (uint32_t)((kk / 4) * C::CH + (kk % 4) * 32); };
       auto issue_s = [&](int it) {  // S^T(it) = K Q^T
@@ -713,25 +1158,27 @@ __global__ void __launch_bounds__(Bwd128::THREADS, 1)
           const uint32_t acc0 = it > 0 ? 1u : 0u;
           if (!b_wait(&bars->p_ready, it & 1, failed)) break;
           tc_fence_after();
-          if (it + 1 < ntiles) {  // S^T(it) has been read: its columns take S^T(it+1)
+          // dV += P^T dO: P of query rows [16 kk, 16 kk + 16) sits at columns 32 (kk / 2) + 8 (kk % 2)
+          const uint64_t bdo0 = smem_desc(do_s, C::CH, 1024, SW_128B);
+#pragma unroll
+          for (int kk = 0; kk < C::BQ / 16; ++kk)
+            mma_ts(tDV, tS + (kk >> 1) * 32 + (kk & 1) * 8, desc_add(bdo0, kk * 16 * 128), id_kv, (acc0 | kk) ? 1u : 0u);
+          if (it + 1 < ntiles) {
+            // S^T(it+1) overwrites the columns dV(it) reads P from: tcgen05.mma
+            // ops of one thread execute in issue order, so no wait is needed.
             if (!b_wait(&bars->q_full[(it + 1) & 1], ((it + 1) >> 1) & 1, failed)) break;
             tc_fence_after();
             issue_s(it + 1);
           }
-          const uint64_t bdo0 = smem_desc(do_s, C::CH, 1024, SW_128B);
-#pragma unroll
-          for (int kk = 0; kk < C::BQ / 16; ++kk)  // dV += P^T dO (K = 128 query rows)
-            mma_ss(tDV, desc_add(dPk0, koff(kk)), desc_add(bdo0, kk * 16 * 128), id_kv, (acc0 | kk) ? 1u : 0u);
-          mma_commit(&bars->dv_done);
           if (!b_wait(&bars->ds_ready, it & 1, failed)) break;
           tc_fence_after();
-          // dK += dS^T Q: dS^T of query rows [16 kk, 16 kk + 16) sits at columns 32 (kk / 2) + 8 (kk % 2)
           const uint64_t bq0 = smem_desc(q_s, C::CH, 1024, SW_128B);
 #pragma unroll
-          for (int kk = 0; kk < C::BQ / 16; ++kk)
-            mma_ts(tDK, tP + (kk >> 1) * 32 + (kk & 1) * 8, desc_add(bq0, kk * 16 * 128), id_kv, (acc0 | kk) ? 1u : 0u);
+          for (int kk = 0; kk < C::BQ / 16; ++kk)  // dK += dS^T Q
+            mma_ss(tDK, desc_add(dSk0, koff(kk)), desc_add(bq0, kk * 16 * 128), id_kv, (acc0 | kk) ? 1u : 0u);
           mma_commit(&bars->q_empty[st]);
-          // dP^T(it+1) overwrites the columns dK(it) reads dS^T from: issue order
+          // dP^T(it) was read before ds_ready; dp_full(it+1) also tells the
+          // elementwise warps that dK(it) is done with the dS tile
           if (it + 1 < ntiles) issue_dp(it + 1);
         }
       }
@@ -745,7 +1192,7 @@ __global__ void __launch_bounds__(Bwd128::THREADS, 1)
     const int n = n0 + r;
     const uint32_t tl = tbase + ((uint32_t)(32 * g) << 16);
     const float scale2 = 2.0f * p.scale;
-    uint8_t* prow = sP + (w4 >> 1) * C::CH + r * 128;
+    uint8_t* dsrow = sDS + (w4 >> 1) * C::CH + r * 128;
     Cursor cur{kvh * G, qt_first};
     for (int it = 0; it < ntiles && !failed; ++it, advance(cur)) {
       const int st = it & 1;
@@ -759,24 +1206,20 @@ __global__ void __launch_bounds__(Bwd128::THREADS, 1)
                              (p.window > 0 && q0g + C::BQ - 1 - n0 >= p.window);
       const float* ir = vVec + st * 256;
       float gv[32];
-      uint32_t pk[16];
       if (need_mask)
-        bwd128_p<BF16, EXACT, true>(tl, w4, ir, scale2, gv, pk, n, q0g, qend, p.Tk, p.window);
+        dkv_p<BF16, EXACT, true>(tl, w4, ir, scale2, gv, n, q0g, qend, p.Tk, p.window);
       else
-        bwd128_p<BF16, EXACT, false>(tl, w4, ir, scale2, gv, pk, n, q0g, qend, p.Tk, p.window);
-      // the P tile is free once dV(it-1) is done
-      if (it > 0 && !b_warp_wait(&bars->dv_done, (it - 1) & 1, failed)) break;
-      bwd128_store_row(prow, w4, r, pk);
-      fence_proxy_async_smem();
+        dkv_p<BF16, EXACT, false>(tl, w4, ir, scale2, gv, n, q0g, qend, p.Tk, p.window);
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->p_ready);
       if (!b_warp_wait(&bars->dp_full, it & 1, failed)) break;
       tc_fence_after();
       if (need_mask)
-        bwd128_ds<BF16, true>(tl + 128, w4, ir, ir + 128, p.scale, gv, n, q0g, qend, p.Tk, p.window);
+        dkv_ds<BF16, true>(tl + 128, w4, dsrow, r, ir, ir + 128, p.scale, gv, n, q0g, qend, p.Tk, p.window);
       else
-        bwd128_ds<BF16, false>(tl + 128, w4, ir, ir + 128, p.scale, gv, n, q0g, qend, p.Tk, p.window);
-      tmem_st_wait();
+        dkv_ds<BF16, false>(tl + 128, w4, dsrow, r, ir, ir + 128, p.scale, gv, n, q0g, qend, p.Tk, p.window);
+      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ds_ready);
     }
@@ -1259,16 +1702,13 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
                       const int64_t* dvs, float scale, int64_t window, cudaStream_t st, int64_t Tk = -1,
                       int64_t qoff = 0, bool det = false) {
   using C = BwdCfg<D>;
-  // D = 128: dQ always comes from the query-major kernel (faster there than the
-  // key-major kernel's fp32 atomics, and deterministic); D = 32 / 64 use it on request
-  if (D == 128) det = true;
-  if (det) dq_acc = nullptr;  // no accumulator
+  if (det) dq_acc = nullptr;  // dQ comes from the query-major kernel: no accumulator
   if (Tk < 0) Tk = T;
   if (((Tk + C::BN - 1) / C::BN) * B * Hkv > INT32_MAX) return SA_ERR_UNSUPPORTED;  // 1-D grid, before any launch
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int64_t rows = B * Hq * T;
   // [B*Hq][ceil(T/64)][3][64] fp32 after delta (sa_flash_bwd_workspace_size counts it)
-  float* rvec = D == 128 ? delta + align256(rows * 4) / 4 : nullptr;
+  float* rvec = D == 128 && det ? delta + align256(rows * 4) / 4 : nullptr;
   int prep_dev = 0, prep_sms = 148;
   if (cudaGetDevice(&prep_dev) == cudaSuccess)
     cudaDeviceGetAttribute(&prep_sms, cudaDevAttrMultiProcessorCount, prep_dev);
@@ -1303,9 +1743,19 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* o
   p.scale = scale;
   dim3 grid((unsigned)(((Tk + C::BN - 1) / C::BN) * B * Hkv));
   if constexpr (D == 128) {
-    auto kern = sp2_bwd128_kernel<BF16, EXACT>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Bwd128::SMEM);
-    kern<<<grid, Bwd128::THREADS, Bwd128::SMEM, st>>>(mq, mk, mv, mdo, p);
+    if (det) {
+      auto kern = sp2_bwd_dkv128_kernel<BF16, EXACT>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DkvCfg::SMEM);
+      kern<<<grid, DkvCfg::THREADS, DkvCfg::SMEM, st>>>(mq, mk, mv, mdo, p);
+    } else {
+      CUtensorMap mq64, mdo64;
+      if (!make_map_4d(&mq64, q, BF16, B, Hq, T, D, qs, 64, Bwd128::BQ) ||
+          !make_map_4d(&mdo64, dout, BF16, B, Hq, T, D, dos, 64, Bwd128::BQ))
+        return SA_ERR_ALIGN;
+      auto kern = sp2_bwd128_kernel<BF16, EXACT>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Bwd128::SMEM);
+      kern<<<grid, Bwd128::THREADS, Bwd128::SMEM, st>>>(mq64, mk, mv, mdo64, p);
+    }
   } else {
     auto kern = det ? sp2_bwd_kernel<D, BF16, EXACT, false> : sp2_bwd_kernel<D, BF16, EXACT, true>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);

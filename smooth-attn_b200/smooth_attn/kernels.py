@@ -630,7 +630,7 @@ def sp2norm_flash_attention(q, k, v, *, scale=None, window_size=0, exact_math=Fa
     D in {32, 64, 128}.  deterministic (an addition to the reference's
     signature; None follows ``torch.use_deterministic_algorithms``): compute
     dQ in the query-major kernel with a fixed summation order, so the
-    backward is bitwise reproducible.  D = 128 always does so.
+    backward is bitwise reproducible.
     """
     assert q.ndim == 4 and k.ndim == 4 and v.ndim == 4
     B, H_q, T, D = q.shape
