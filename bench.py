@@ -324,8 +324,10 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
     except (ValueError, RuntimeError) as e:
         return {"unavailable": str(e)[:200]}
 
-    def step():
-        o = sa.sp2norm_flash_attention(q, k, v)
+    det = bool(getattr(args, "deterministic", False))
+
+    def step(det=det):
+        o = sa.sp2norm_flash_attention(q, k, v, deterministic=det)
         torch.autograd.grad(o, (q, k, v), do)  # fresh dq/dk/dv, no .grad accumulation kernels
 
     for _ in range(max(args.warmup, 3)):
@@ -343,6 +345,10 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
     fsteps = max(3, steps // 3)
     fwd_ms = time_steps(lambda: sa.sp2norm_flash_attention(q.detach(), k.detach(), v.detach()), fsteps, world) / fsteps
     fwd_flops_loc = O.flash_flops(1, b_loc, T, D)
+    # the bitwise-reproducible backward (query-major dQ) on the same inputs (short region)
+    for _ in range(3):
+        step(not det)
+    other_ms = time_steps(lambda: step(not det), fsteps, world) / fsteps
     return {
         "metric": "fused squareplus-attn fwd+bwd TFLOP/s", "value": round(flops_all / (ms * 1e-3) / 1e12, 1),
         "unit": "TFLOP/s", "ms_per_step": round(ms, 3), "steps": steps,
@@ -356,6 +362,9 @@ def run_flash(args, world, rank, tf_burst, tf_sus, peak_kind):
         "clocks": clk.summary(),
         "fwd_only": {"ms": round(fwd_ms, 3), "tflops": round(fwd_flops_loc / (fwd_ms * 1e-3) / 1e12, 1),
                      "frac_of_burst": round(fwd_flops_loc / (fwd_ms * 1e-3) / 1e12 / tf_burst, 4)},
+        "deterministic": det,
+        ("atomic_dq" if det else "deterministic_dq"): {
+            "ms": round(other_ms, 3), "tflops": round(flops_loc / (other_ms * 1e-3) / 1e12, 1)},
     }
 
 
@@ -793,6 +802,8 @@ def main():
     ap.add_argument("--flash-shape", default=",".join(str(FLASH_CFG[k]) for k in "BHTD"),
                     help="B,H,T,D of the attention workload (BASELINE: 4,32,4096,128)")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="flash fwd+bwd through the bitwise-reproducible backward (query-major dQ)")
     ap.add_argument("--skip-extra", action="store_true", help="skip the other BASELINE configs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--flash-seconds", type=float, default=2.0,
