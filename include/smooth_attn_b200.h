@@ -35,6 +35,7 @@ extern "C" {
 #define SA_ERR_LAUNCH (-4)      /* CUDA launch error (cudaGetLastError)        */
 #define SA_ERR_TIMEOUT (-5)     /* a bounded device-side wait gave up          */
 #define SA_ERR_CUDA (-6)        /* other CUDA runtime/driver error             */
+#define SA_ERR_BOUNDS (-7)      /* debug build: a device-side index check failed */
 
 /* Element types. */
 #define SA_F32 0
@@ -54,8 +55,9 @@ SA_API const char* sa_last_cuda_error(void);
  * Device-side status of the current device: SA_ERR_TIMEOUT if any kernel of
  * this library gave up a bounded wait (an mbarrier / copy that never
  * completed) since the last reset, else SA_OK.  Synchronises the device.
- * Otherwise SA_ERR_ARG if sa_paged_decode met a block_table entry outside
- * [0, num_blocks) since the last reset.
+ * Otherwise SA_ERR_BOUNDS if (debug library only) a device-side index check
+ * failed, otherwise SA_ERR_ARG if sa_paged_decode met a block_table entry
+ * outside [0, num_blocks) since the last reset.
  * reset != 0 clears the recorded status.  (No reference counterpart: the
  * reference's Triton kernels have no bounded waits.)
  */
@@ -80,6 +82,13 @@ SA_API int sa_stream_status(void* stream, int reset);
  * reference counterpart: the reference's kernels have no bounded waits.)
  */
 SA_API int sa_probe_bounded_wait(int64_t limit_ns, int* done, void* stream);
+
+/*
+ * 1 if this library was built with device-side index checks (the debug
+ * library, libsmooth_attn_b200_debug.so), else 0.  Host only.  (No reference
+ * counterpart: the reference has no debug build.)
+ */
+SA_API int sa_debug_checks(void);
 
 /*
  * Squareplus normalization forward over rows of length `cols`.

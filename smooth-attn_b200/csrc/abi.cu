@@ -21,6 +21,15 @@ int paged_bad_pages(int reset, cudaStream_t st);     // paged.cu
 int paged_tc_timeouts(int reset, cudaStream_t st);   // paged_tc.cu
 int paged_tc_bad_pages(int reset, cudaStream_t st);  // paged_tc.cu
 int proj_timeouts(int reset, cudaStream_t st);       // proj.cu
+// index checks that failed, per file (debug library; always 0 in release)
+int norm_bounds(int reset, cudaStream_t st);
+int flash_fwd_bounds(int reset, cudaStream_t st);
+int flash_bwd_bounds(int reset, cudaStream_t st);
+int paged_bounds(int reset, cudaStream_t st);
+int paged_tc_bounds(int reset, cudaStream_t st);
+int rope_bounds(int reset, cudaStream_t st);
+int fp8_bounds(int reset, cudaStream_t st);
+int proj_bounds(int reset, cudaStream_t st);
 
 // Waits that the probe kernel below gave up on.
 __device__ unsigned g_probe_timeouts;
@@ -60,7 +69,10 @@ static int collect(int reset, cudaStream_t st) {
                 paged_timeouts(reset, st) + paged_tc_timeouts(reset, st) + probe_timeouts(reset, st) +
                 proj_timeouts(reset, st);
   const int bad = paged_bad_pages(reset, st) + paged_tc_bad_pages(reset, st);
-  return n ? SA_ERR_TIMEOUT : bad ? SA_ERR_ARG : SA_OK;
+  const int oob = norm_bounds(reset, st) + flash_fwd_bounds(reset, st) + flash_bwd_bounds(reset, st) +
+                  paged_bounds(reset, st) + paged_tc_bounds(reset, st) + rope_bounds(reset, st) +
+                  fp8_bounds(reset, st) + proj_bounds(reset, st);
+  return n ? SA_ERR_TIMEOUT : oob ? SA_ERR_BOUNDS : bad ? SA_ERR_ARG : SA_OK;
 }
 }  // namespace sa
 
@@ -84,6 +96,14 @@ extern "C" int sa_probe_bounded_wait(int64_t limit_ns, int* done, void* stream) 
 
 extern "C" int sa_version(void) { return (0 << 16) | 1; }
 
+extern "C" int sa_debug_checks(void) {
+#ifdef SA_DEBUG_CHECKS
+  return 1;
+#else
+  return 0;
+#endif
+}
+
 extern "C" const char* sa_last_cuda_error(void) { return g_last_err; }
 
 extern "C" const char* sa_status_string(int status) {
@@ -95,6 +115,7 @@ extern "C" const char* sa_status_string(int status) {
     case SA_ERR_LAUNCH: return "CUDA launch failed";
     case SA_ERR_TIMEOUT: return "device-side wait timed out";
     case SA_ERR_CUDA: return "CUDA error";
+    case SA_ERR_BOUNDS: return "device-side index check failed (debug build)";
     default: return "unknown status";
   }
 }

@@ -779,6 +779,7 @@ __global__ void __launch_bounds__(448, 1)
       mbar_arrive(&bars->dq_free);
       const int h = cur.h;
       const int q0 = cur.qt * C::BQ;
+      if (!SA_DCHECK(h < p.Hq && q0 < p.T)) continue;  // the dQ rows of a query tile that exists
       float* dst = p.dq_acc + (((int64_t)b * p.Hq + h) * p.T + q0) * D + d;
       const int lim = p.T - q0;
 #pragma unroll
@@ -1120,6 +1121,7 @@ __global__ void __launch_bounds__(DkvCfg::THREADS, 1)
           tma_load_4d(sQ + st * C::TILE + c * C::CH, &tmq, c * 64, q0, h, b, &bars->q_full[st]);
           tma_load_4d(sDO + st * C::TILE + c * C::CH, &tmdo, c * 64, q0, h, b, &bars->q_full[st]);
         }
+        (void)SA_DCHECK(h < p.Hq && cur.qt < ntq);  // a constants block the prep kernel wrote
         bulk_g2s(vVec + st * 256, p.rvec + (((int64_t)b * p.Hq + h) * ntq + cur.qt) * 256, C::VEC_TILE,
                  &bars->q_full[st]);
       }
@@ -2025,3 +2027,4 @@ extern "C" int sa_flash_bwd_noalloc(const void* q, const void* k, const void* v,
                       q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides, dk_strides, dv_strides,
                       scale, window_size, exact_math, dtype, 0, stream);
 }
+SA_BOUNDS_ACCESSOR(flash_bwd_bounds)

@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(320, 1)
                       &bars->q_full);
       for (int i = 0; i < j1 - j0 && !failed; ++i) {
         const int kv0 = (j0 + i) * C::BN;
+        (void)SA_DCHECK(kv0 < p.Tk && kv0 <= qbase + p.qoff + 2 * C::BM - 1);  // a key tile some query sees
         const int ks = i % C::NK, vs = i % C::NV;
         if (i >= C::NK && !wait_or_flag(&bars->k_empty[ks], ((i / C::NK) - 1) & 1, failed)) break;
         mbar_arrive_expect_tx(&bars->k_full[ks], C::QK_TILE);
@@ -661,3 +662,4 @@ extern "C" int sa_fp8_flash_fwd(const void* q8, const void* k8, const void* vq, 
   if (rc != SA_OK) return rc;
   return sa_record_cuda_error(cudaGetLastError());
 }
+SA_BOUNDS_ACCESSOR(flash_fwd_bounds)

@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(Fp8Src s, const unsig
     const T* x = static_cast<const T*>(s.p[t]);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < s.n[t] / 8; i += stride) {
       float f[8];
+      if (!SA_DCHECK(i * 8 + 8 <= s.n[t])) continue;
       load8<T>(x + i * 8, f);
       uint8_t b[8];
 #pragma unroll
@@ -165,3 +166,4 @@ extern "C" int sa_fp8_quantize(const void* q, const void* k, const void* v, int6
     default: return sa::launch_fp8_quantize<__nv_bfloat16>(s, amax, q8p, k8p, vqp, scales, st);
   }
 }
+SA_BOUNDS_ACCESSOR(fp8_bounds)

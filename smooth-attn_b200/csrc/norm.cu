@@ -268,7 +268,8 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_fwd_bulk(const T* __rest
 
   auto issue = [&](int64_t row, int s) {
     const int q = CAUSAL ? (int)(row % cols) : cols - 1;
-    const uint32_t bytes = (uint32_t)((q + VEC) / VEC) * 16u;
+    uint32_t bytes = (uint32_t)((q + VEC) / VEC) * 16u;
+    if (!SA_DCHECK(bytes <= (uint32_t)sb && row < rows)) bytes = 16u;  // the row must fit its ring slot
     mbar_arrive_expect_tx(&bars[s], bytes);
     bulk_g2s(ring + (size_t)s * sb, x + row * ldx, bytes, &bars[s]);
   };
@@ -410,8 +411,9 @@ __global__ void __launch_bounds__(kBulkWarps * 32) norm_bwd_bulk(const T* __rest
   auto issue = [&](int64_t row, int s) {
     const int q = CAUSAL ? (int)(row % cols) : cols - 1;
     const int nv = (q + VEC) / VEC;
-    const uint32_t bx = (uint32_t)nv * 16u;
-    const uint32_t bg = ((uint32_t)nv * GB + 15u) & ~15u;  // in-row: cols*sizeof(TG) % 16 == 0
+    uint32_t bx = (uint32_t)nv * 16u;
+    uint32_t bg = ((uint32_t)nv * GB + 15u) & ~15u;  // in-row: cols*sizeof(TG) % 16 == 0
+    if (!SA_DCHECK(bx <= (uint32_t)gofs && (uint32_t)gofs + bg <= (uint32_t)sb && row < rows)) bx = bg = 16u;  // x and dY fit the slot
     mbar_arrive_expect_tx(&bars[s], bx + bg);
     bulk_g2s(ring + (size_t)s * sb, x + row * ldx, bx, &bars[s]);
     bulk_g2s(ring + (size_t)s * sb + gofs, g + row * ldg, bg, &bars[s]);
@@ -844,3 +846,4 @@ extern "C" int sa_norm_bwd(const void* x, const void* g, const float* rowsum, vo
 #undef SA_BWD_G
   return sa_record_cuda_error(cudaGetLastError());
 }
+SA_BOUNDS_ACCESSOR(norm_bounds)

@@ -162,6 +162,8 @@ __global__ void __launch_bounds__(kPgWarps * 32) paged_decode_kernel(const Paged
       atomicAdd(&g_paged_bad_pages, 1u);
       phys = 0;
     }
+    // the chunk lies inside its page and the KV head exists
+    if (!SA_DCHECK(h < a.Hkv && sub < a.cpp && (int64_t)(sub + 1) * a.CR <= a.bs)) return;  // wait then gives up
     const int64_t off = (((int64_t)phys * a.Hkv + h) * a.bs + (int64_t)sub * a.CR) * D;
     uint8_t* slot = ring + (size_t)s * a.stage;
     mbar_arrive_expect_tx(&bars[s], 2u * chunk_bytes);
@@ -689,3 +691,4 @@ extern "C" int sa_paged_decode(const void* q, const void* k_cache, const void* v
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == SA_BF16 ? sa::launch_dt<__nv_bfloat16>(D, a, p, st) : sa::launch_dt<__half>(D, a, p, st);
 }
+SA_BOUNDS_ACCESSOR(paged_bounds)

@@ -257,6 +257,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!isv) atomicAdd(&g_ptc_bad_pages, 1u);
           phys = 0;
         }
+        (void)SA_DCHECK(nload >= 1 && nload <= np && p0 + nload <= a.max_blocks);  // pages of this tile
         if (n >= NS && !wait_uni(&empty[s], ((n / NS) - 1) & 1, failed)) break;
         if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)nload * a.bs * D * 2);
         __syncwarp();
@@ -616,3 +617,4 @@ int paged_tc_launch(const void* q, const void* k_cache, const void* v_cache, voi
 }
 
 }  // namespace sa
+SA_BOUNDS_ACCESSOR(paged_tc_bounds)

@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int it = 0;  // ring position over all (tile, k-step) pairs of this CTA
       for (int t = blockIdx.x; t < ntiles && !failed; t += gridDim.x) {
         const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * BN;
+        (void)SA_DCHECK(m0 < p.M && n0 < p.N);  // the tile starts inside the output
         for (int kb = 0; kb < nk && !failed; ++kb, ++it) {
           const int s = it % NST;
           if (it >= NST && !wait_or_flag(&bars->empty[s], ((it / NST) - 1) & 1, failed)) break;
@@ -263,3 +264,4 @@ extern "C" int sa_out_proj(const void* a, const void* w, void* out, int64_t M, i
   }
   return sa_record_cuda_error(cudaGetLastError());
 }
+SA_BOUNDS_ACCESSOR(proj_bounds)

@@ -66,6 +66,7 @@ __global__ void __launch_bounds__(256) rope_rotate_kernel(RopeTensor a, RopeTens
     const int64_t t = row % T;
     const int64_t bh = row / T;
     const int64_t h = bh % r.H, bb = bh / r.H;
+    if (!SA_DCHECK(bb < B && g * 8 + 8 <= D / 2)) continue;
     const E* xr = static_cast<const E*>(r.x) + bb * r.sb + h * r.sh + t * r.st;
     E* orow = static_cast<E*>(r.out) + row * D;
     float x1[8], x2[8], c[8], s[8];
@@ -176,3 +177,4 @@ extern "C" int sa_rope_flash_fwd(const void* q, const void* k, const void* v, vo
   return sa_flash_fwd(qr, kr, v, o, nullptr, rowsum, B, Hq, Hkv, T, D, qs, ks, v_strides, o_strides, scale, window_size,
                       exact_math, dtype, stream);
 }
+SA_BOUNDS_ACCESSOR(rope_bounds)

@@ -12,6 +12,37 @@
 
 #define SA_EPS 1e-12f  // src/smooth_attn/kernels.py:57
 
+// ---- debug build: device-side index checks ------------------------------------
+// `python smooth-attn_b200/build.py --debug` compiles every kernel with
+// SA_DEBUG_CHECKS into libsmooth_attn_b200_debug.so (loaded when the
+// environment sets SA_DEBUG_LIB=1).  There SA_DCHECK(cond) tests an index
+// invariant; a failure adds one to this file's counter, and the caller skips
+// or clamps the access.  Nothing traps.  sa_device_status / sa_stream_status
+// report any failure as SA_ERR_BOUNDS.  In the release library the checks
+// compile to `true`.
+static __device__ unsigned sa_g_bounds;  // one per file: only this file's kernels add to it
+#ifdef SA_DEBUG_CHECKS
+#define SA_DCHECK(cond) ((cond) ? true : (atomicAdd(&::sa_g_bounds, 1u), false))
+#else
+#define SA_DCHECK(cond) true
+#endif
+// Host side: `int NAME(int reset, cudaStream_t st)` reads (and optionally
+// clears) this file's counter, stream-ordered.
+#define SA_BOUNDS_ACCESSOR(NAME)                                                                 \
+  namespace sa {                                                                                 \
+  int NAME(int reset, cudaStream_t st) {                                                         \
+    unsigned v = 0;                                                                              \
+    cudaMemcpyFromSymbolAsync(&v, ::sa_g_bounds, sizeof(v), 0, cudaMemcpyDeviceToHost, st);      \
+    cudaStreamSynchronize(st);                                                                   \
+    if (reset) {                                                                                 \
+      const unsigned z = 0;                                                                      \
+      cudaMemcpyToSymbolAsync(::sa_g_bounds, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st);      \
+      cudaStreamSynchronize(st);                                                                 \
+    }                                                                                            \
+    return (int)v;                                                                               \
+  }                                                                                              \
+  }
+
 namespace sa {
 
 // ---- element conversion ----------------------------------------------------

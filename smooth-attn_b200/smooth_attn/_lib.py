@@ -9,10 +9,13 @@ library is missing or cannot be loaded, every kernel entry point raises
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 LIB_PATH = Path(__file__).with_name("libsmooth_attn_b200.so")
+# SA_DEBUG_LIB=1: the debug build (device-side index checks, build.py --debug)
+DEBUG_LIB_PATH = Path(__file__).with_name("libsmooth_attn_b200_debug.so")
 
 SA_OK = 0
 SA_ERR_ARG = -1
@@ -21,6 +24,7 @@ SA_ERR_UNSUPPORTED = -3
 SA_ERR_LAUNCH = -4
 SA_ERR_TIMEOUT = -5
 SA_ERR_CUDA = -6
+SA_ERR_BOUNDS = -7
 
 SA_F32, SA_F16, SA_BF16 = 0, 1, 2
 
@@ -38,6 +42,7 @@ SIGNATURES = {
     "sa_device_status": (_int, [_int]),
     "sa_stream_status": (_int, [_p, _int]),
     "sa_probe_bounded_wait": (_int, [_i64, _p, _p]),
+    "sa_debug_checks": (_int, []),
     "sa_norm_fwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _int, _int, _f, _f, _int, _p]),
     "sa_norm_bwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _f, _f, _int, _p]),
     "sa_flash_fwd": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
@@ -82,7 +87,10 @@ def load(path: Path | str | None = None):
     with _lock:
         if _lib is not None and path is None:
             return _lib
-        p = Path(path) if path is not None else LIB_PATH
+        if path is not None:
+            p = Path(path)
+        else:
+            p = DEBUG_LIB_PATH if os.environ.get("SA_DEBUG_LIB", "") not in ("", "0") else LIB_PATH
         if not p.exists():
             raise RuntimeError(
                 f"{p.name} is not built (expected at {p}); run `python smooth-attn_b200/build.py`. "

@@ -154,6 +154,18 @@ def test_c_abi_library_exports_every_header_symbol():
     assert set(syms) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
     assert lib.sa_version() >= 1
     assert lib.sa_status_string(_lib.SA_ERR_ARG) == b"invalid argument"
+    assert lib.sa_debug_checks() == 0  # the release library has no device-side index checks
+
+
+def test_debug_library_exports_every_header_symbol():
+    """build.py --debug (run by the driver's build step) gives the same ABI with the checks compiled in."""
+    if not _lib.DEBUG_LIB_PATH.exists():
+        pytest.skip("debug library not built (python smooth-attn_b200/build.py --debug)")
+    dbg = _lib.load(_lib.DEBUG_LIB_PATH)
+    for s in _header_symbols():
+        assert hasattr(dbg, s), s
+    assert dbg.sa_debug_checks() == 1
+    assert dbg.sa_status_string(_lib.SA_ERR_BOUNDS) == b"device-side index check failed (debug build)"
 
 
 def test_c_abi_rejects_bad_arguments_before_launch():
