@@ -112,6 +112,32 @@ SA_API int sa_norm_fwd(const void* x, void* out, float* rowsum, int64_t rows, in
                 int64_t ld_out, int dtype, int causal, float alpha, float theta, int power, void* stream);
 
 /*
+ * Host <-> device copy of the part of causal [nmat, L, L] matrices that the
+ * causal norm reads (to_device != 0) or that can be nonzero in its output
+ * (to_device == 0): for every band of `band` rows (a multiple of 8; the last
+ * band may be shorter), rows [r0, r1) x columns [0, min(L, r1 rounded up to
+ * 16 bytes)) of every matrix.  One cudaMemcpy3DAsync per band covers all
+ * nmat matrices; src and dst are contiguous [nmat, L, L] with elem_bytes-byte
+ * elements, the host side pinned.  The columns past each band's width are
+ * neither read nor written.  Returns the bytes one call moves through
+ * *bytes_out (nullable).  (No reference counterpart: the reference has no
+ * host-buffer path; smooth_attn.host uses this to move about half of the
+ * matrix bytes over PCIe in each direction.)
+ */
+SA_API int sa_copy_causal_bands(void* dst, const void* src, int64_t nmat, int64_t L, int64_t elem_bytes,
+                                int64_t band, int to_device, int64_t* bytes_out, void* stream);
+
+/*
+ * Host memory: writes zeros to the part of [nmat, L, L] matrices that
+ * sa_copy_causal_bands (to_device == 0) does not write -- in each band, the
+ * columns past the band's copied width -- with `nthreads` host threads
+ * (<= 0: one per core, at most 32) and non-temporal stores where the CPU has
+ * them.  Blocks until done.  No GPU call.  (No reference counterpart.)
+ */
+SA_API int sa_host_zero_causal_tail(void* out, int64_t nmat, int64_t L, int64_t elem_bytes, int64_t band,
+                                    int nthreads);
+
+/*
  * Fused backward of sa_norm_fwd.
  *   dx_j = (dy_j/dx_j / S) * (g_j - sum_k g_k y_k / S),  S = sum_k y_k + 1e-12
  *   dy/dx = alpha * power * sp^(power-1) * sp',  sp' = (1 + a / sqrt(a^2+4)) / 2

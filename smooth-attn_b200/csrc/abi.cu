@@ -1,6 +1,14 @@
-// C-ABI utilities: version, status strings, last CUDA error (per thread).
+// C-ABI utilities: version, status strings, last CUDA error (per thread),
+// and the host-buffer helpers of the causal norm's host path.
 #include <stdio.h>
 #include <string.h>
+
+#include <algorithm>
+#include <thread>
+#include <vector>
+#if defined(__x86_64__)
+#include <emmintrin.h>
+#endif
 
 #include "sa_common.cuh"
 
@@ -95,6 +103,82 @@ extern "C" int sa_probe_bounded_wait(int64_t limit_ns, int* done, void* stream) 
 }
 
 extern "C" int sa_version(void) { return (0 << 16) | 1; }
+
+extern "C" int sa_copy_causal_bands(void* dst, const void* src, int64_t nmat, int64_t L, int64_t elem_bytes,
+                                    int64_t band, int to_device, int64_t* bytes_out, void* stream) {
+  if (bytes_out != nullptr) *bytes_out = 0;
+  if (nmat < 0 || L < 0 || band <= 0 || band % 8 != 0 || (elem_bytes != 2 && elem_bytes != 4)) return SA_ERR_ARG;
+  if (nmat == 0 || L == 0) return SA_OK;
+  if (dst == nullptr || src == nullptr) return SA_ERR_ARG;
+  const int64_t vec = 16 / elem_bytes;
+  const size_t pitch = (size_t)(L * elem_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t moved = 0;
+  for (int64_t r0 = 0; r0 < L; r0 += band) {
+    const int64_t r1 = r0 + band < L ? r0 + band : L;
+    int64_t w = (r1 + vec - 1) / vec * vec;
+    if (w > L) w = L;
+    cudaMemcpy3DParms cp = {};
+    // pitched pointers whose "height" is L rows, so one depth step is one whole matrix
+    cp.srcPtr = make_cudaPitchedPtr(const_cast<char*>(static_cast<const char*>(src)) + r0 * pitch, pitch,
+                                    (size_t)(w * elem_bytes), (size_t)L);
+    cp.dstPtr = make_cudaPitchedPtr(static_cast<char*>(dst) + r0 * pitch, pitch, (size_t)(w * elem_bytes), (size_t)L);
+    cp.extent = make_cudaExtent((size_t)(w * elem_bytes), (size_t)(r1 - r0), (size_t)nmat);
+    cp.kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+    const cudaError_t e = cudaMemcpy3DAsync(&cp, st);
+    if (e != cudaSuccess) return sa_record_cuda_error(e);
+    moved += (r1 - r0) * w * elem_bytes * nmat;
+  }
+  if (bytes_out != nullptr) *bytes_out = moved;
+  return SA_OK;
+}
+
+// Zeros [p, p + bytes): 16-byte non-temporal stores for the aligned middle
+// (no read-for-ownership of lines that are only overwritten), memset around it.
+static void zero_bytes(char* p, size_t bytes) {
+#if defined(__x86_64__)
+  char* a = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+  if (a > p + bytes) a = p + bytes;
+  memset(p, 0, (size_t)(a - p));
+  const size_t mid = (bytes - (size_t)(a - p)) & ~size_t(15);
+  const __m128i z = _mm_setzero_si128();
+  for (size_t i = 0; i < mid; i += 16) _mm_stream_si128(reinterpret_cast<__m128i*>(a + i), z);
+  memset(a + mid, 0, bytes - (size_t)(a - p) - mid);
+#else
+  memset(p, 0, bytes);
+#endif
+}
+
+extern "C" int sa_host_zero_causal_tail(void* out, int64_t nmat, int64_t L, int64_t elem_bytes, int64_t band,
+                                        int nthreads) {
+  if (nmat < 0 || L < 0 || band <= 0 || band % 8 != 0 || (elem_bytes != 2 && elem_bytes != 4)) return SA_ERR_ARG;
+  if (nmat == 0 || L == 0) return SA_OK;
+  if (out == nullptr) return SA_ERR_ARG;
+  int nt = nthreads > 0 ? nthreads : (int)std::thread::hardware_concurrency();
+  nt = std::max(1, std::min(nt, 32));
+  nt = (int)std::min<int64_t>(nt, nmat);
+  const int64_t vec = 16 / elem_bytes;
+  auto work = [&](int64_t m0, int64_t m1) {
+    for (int64_t m = m0; m < m1; ++m) {
+      char* base = static_cast<char*>(out) + (size_t)m * (size_t)(L * L * elem_bytes);
+      for (int64_t r0 = 0; r0 < L; r0 += band) {
+        const int64_t r1 = std::min(L, r0 + band);
+        const int64_t w = std::min(L, (r1 + vec - 1) / vec * vec);
+        if (w >= L) continue;
+        for (int64_t r = r0; r < r1; ++r)
+          zero_bytes(base + (size_t)(r * L + w) * (size_t)elem_bytes, (size_t)((L - w) * elem_bytes));
+      }
+    }
+#if defined(__x86_64__)
+    _mm_sfence();  // the streaming stores are globally visible before this thread is joined
+#endif
+  };
+  std::vector<std::thread> th;
+  for (int t = 1; t < nt; ++t) th.emplace_back(work, nmat * t / nt, nmat * (t + 1) / nt);
+  work(0, nmat / nt);
+  for (auto& x : th) x.join();
+  return SA_OK;
+}
 
 extern "C" int sa_debug_checks(void) {
 #ifdef SA_DEBUG_CHECKS

@@ -43,6 +43,8 @@ SIGNATURES = {
     "sa_stream_status": (_int, [_p, _int]),
     "sa_probe_bounded_wait": (_int, [_i64, _p, _p]),
     "sa_debug_checks": (_int, []),
+    "sa_copy_causal_bands": (_int, [_p, _p, _i64, _i64, _i64, _i64, _int, _i64p, _p]),
+    "sa_host_zero_causal_tail": (_int, [_p, _i64, _i64, _i64, _i64, _int]),
     "sa_norm_fwd": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _int, _int, _f, _f, _int, _p]),
     "sa_norm_bwd": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _f, _f, _int, _p]),
     "sa_flash_fwd": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,

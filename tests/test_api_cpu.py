@@ -2,6 +2,7 @@
 reference's error conventions, the eager functions, and the C ABI library's
 exported symbols."""
 
+import ctypes
 import re
 from pathlib import Path
 
@@ -182,3 +183,39 @@ def test_c_abi_rejects_bad_arguments_before_launch():
     assert lib.sa_norm_bwd(null, null, null, null, 4, 4, 4, 4, 4, 0, 9, 1, 2.0, 0.5, 2, null) == _lib.SA_ERR_UNSUPPORTED
     with pytest.raises(ValueError):
         _lib.check(_lib.SA_ERR_ARG, "sa_norm_fwd")
+
+
+def test_band_copy_rejects_bad_arguments_before_any_copy():
+    lib = _lib.load()
+    n = ctypes.c_int64(-1)
+    assert lib.sa_copy_causal_bands(None, None, 2, 64, 2, 12, 1, ctypes.byref(n), None) == _lib.SA_ERR_ARG  # band % 8
+    assert lib.sa_copy_causal_bands(None, None, 2, 64, 3, 128, 1, None, None) == _lib.SA_ERR_ARG  # element size
+    assert lib.sa_copy_causal_bands(None, None, 2, 64, 2, 128, 1, None, None) == _lib.SA_ERR_ARG  # null pointers
+    assert lib.sa_copy_causal_bands(None, None, 0, 64, 2, 128, 1, ctypes.byref(n), None) == _lib.SA_OK
+    assert n.value == 0
+
+
+def test_host_path_needs_pinned_cpu_tensors():
+    from smooth_attn import host
+
+    x = torch.randn(1, 16, 16)
+    with pytest.raises(ValueError):
+        sa.softplus_norm_causal_host_out(torch.empty_like(x), x)  # not pinned
+    with pytest.raises(TypeError):
+        sa.softplus_norm_causal_host_out(None, x)
+    assert host.causal_band_bytes((8, 16, 2048, 2048), torch.bfloat16) == 570425344
+
+
+@pytest.mark.parametrize(("L", "elem"), [(300, 2), (2048, 2), (129, 4), (7, 2)])
+def test_host_zero_causal_tail_writes_exactly_the_tail(L, elem):
+    """Host-only: zeros the columns past each 128-row band's copied width, nothing else."""
+    from smooth_attn import host
+
+    dt = np.uint16 if elem == 2 else np.uint32
+    a = np.full((3, L, L), 0xABCD, dtype=dt)
+    st = _lib.load().sa_host_zero_causal_tail(ctypes.c_void_p(a.ctypes.data), 3, L, elem, host.BAND, 3)
+    assert st == _lib.SA_OK
+    want = np.full((3, L, L), 0xABCD, dtype=dt)
+    for r0, r1, w in host._bands(L, elem):
+        want[:, r0:r1, w:] = 0
+    assert np.array_equal(a, want)
