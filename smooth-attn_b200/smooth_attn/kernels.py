@@ -295,6 +295,30 @@ def sp2norm_triton(x, return_meta=False):
 # ---------------------------------------------------------------------------
 
 
+_FAST_CODES = {torch.float32: _lib.SA_F32, torch.float16: _lib.SA_F16, torch.bfloat16: _lib.SA_BF16}
+_DEFAULT_ARGS = (float(DEFAULT_FAMILY.alpha), float(DEFAULT_FAMILY.theta), int(DEFAULT_FAMILY.power))
+
+
+def _causal_out_fast(out, x):
+    """Launch the default-family causal forward for plain contiguous CUDA
+    tensors of one shape / dtype / device; None when the call needs the
+    general path (tracing, other layouts, anything to validate or report)."""
+    code = _FAST_CODES.get(x.dtype)
+    if (code is None or not x.is_cuda or x.dim() < 2 or out.dtype is not x.dtype or out.shape != x.shape
+            or not x.is_contiguous() or not out.is_contiguous() or out.device != x.device):
+        return None
+    L = x.shape[-1]
+    if L != x.shape[-2] or L > MAX_ROW_COLS or L == 0 or torch.compiler.is_compiling() or _get_proxy_mode() is not None:
+        return None
+    dev = x.device.index
+    if dev != torch.cuda.current_device():
+        return None
+    st = _lib.load().sa_norm_fwd(x.data_ptr(), out.data_ptr(), None, x.numel() // L, L, L, L, code, 1,
+                                 *_DEFAULT_ARGS, ctypes.c_void_p(torch._C._cuda_getCurrentRawStream(dev)))
+    _lib.check(st, "sa_norm_fwd")
+    return out
+
+
 def _causal_out(out, x_attn, family, rowsum=None):
     kernel_out, user_out = _prepare_output(out, x_attn)
     L = x_attn.shape[-1]
@@ -319,6 +343,14 @@ def softplus_norm_causal_triton(x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAM
 
 def softplus_norm_causal_triton_out(out, x, alpha=DEFAULT_FAMILY.alpha, theta=DEFAULT_FAMILY.theta,
                                     power=DEFAULT_FAMILY.power, *, family=None, return_meta=False):
+    if (family is None and not return_meta and type(x) is torch.Tensor and type(out) is torch.Tensor
+            and alpha is DEFAULT_FAMILY.alpha and theta is DEFAULT_FAMILY.theta and power is DEFAULT_FAMILY.power):
+        # the common call (default family, contiguous same-shape CUDA tensors) without the general
+        # path's per-call objects; anything else, or any check failing, takes the general path
+        # below with its full validation and error messages
+        done = _causal_out_fast(out, x)
+        if done is not None:
+            return done
     family = _resolve_family(alpha, theta, power, family)
     x_attn = _prepare_attention_input(x)
     result, meta = _causal_out(out, x_attn, family)
