@@ -345,3 +345,19 @@ def test_flash_bwd_chunk_deterministic():
     emu = O.chunk_flash_attention_bwd(*args, window_size=96, emulate=True)
     for g, r, m in zip(got, ref, emu):
         check_bf16_grads(np32(g), r, m, **BWD_TOL)
+
+
+@pytest.mark.parametrize(("Hq", "Hkv", "T", "D", "W"), [(4, 2, 200, 64, 0), (4, 1, 333, 128, 90)])
+def test_flash_bwd_deterministic_exact_math(Hq, Hkv, T, D, W):
+    """The deterministic kernels with IEEE sqrt (exact_math) against the oracle, and bitwise repeatable."""
+    q, k, v = _qkv(1, Hq, Hkv, T, D, seed=T + 11)
+    do = randn((1, Hq, T, D), T + 12, torch.bfloat16, CUDA)
+
+    def grads():
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+        sa.sp2norm_flash_attention(qq, kk, vv, window_size=W, exact_math=True, deterministic=True).backward(do)
+        return qq.grad, kk.grad, vv.grad
+
+    a, b = grads(), grads()
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    _check_grads(a, q, k, v, do, window=W)
