@@ -922,11 +922,9 @@ struct DkvCfg {
   static constexpr int OFF_DS = OFF_DO + NS * TILE;  // dS [kv 128][q 128] as two 64-query chunks
   static constexpr int OFF_VEC = OFF_DS + TILE;
   static constexpr int OFF_BAR = OFF_VEC + NS * VEC_TILE;
-  // The tiles start at the first 1024-byte boundary of dynamic shared memory
-  // (up to 1008 bytes in, for a 16-byte-aligned start); the 128-byte barrier
-  // block goes in front of them when that gap holds it, else right after
-  // them, and either way inside the allocation.
-  static constexpr int SMEM = OFF_BAR + 1024;
+  // no alignment slack: the kernel checks that dynamic shared memory starts
+  // on a 1024-byte boundary (it does when the kernel has no static shared data)
+  static constexpr int SMEM = OFF_BAR + 128;
   static constexpr int EW = 512;  // elementwise threads
   static constexpr int THREADS = EW + 64;
   static_assert(SMEM <= 227 * 1024, "shared memory plan");
@@ -1036,15 +1034,19 @@ __global__ void __launch_bounds__(DkvCfg::THREADS, 1)
                       BwdParams p) {
   using C = DkvCfg;
   constexpr int D = C::D;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // never expected; all threads leave before any barrier
+    if (threadIdx.x == 0) atomicAdd(&g_flash_bwd_timeouts, 1u);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* sK = smem + C::OFF_K;
   uint8_t* sV = smem + C::OFF_V;
   uint8_t* sQ = smem + C::OFF_Q;
   uint8_t* sDO = smem + C::OFF_DO;
   uint8_t* sDS = smem + C::OFF_DS;
   float* vVec = reinterpret_cast<float*>(smem + C::OFF_VEC);  // [NS][2][128]
-  DkvBars* bars = reinterpret_cast<DkvBars*>(smem - smem_raw >= 128 ? smem_raw : smem + C::OFF_BAR);
+  DkvBars* bars = reinterpret_cast<DkvBars*>(smem + C::OFF_BAR);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int kvt, bhk;  // KV tile (0 = most query tiles) and (batch, kv head)
