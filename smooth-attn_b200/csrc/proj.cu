@@ -76,8 +76,15 @@ __device__ __forceinline__ bool warp_wait_or_flag(uint64_t* bar, uint32_t phase,
 template <bool BF16>
 __global__ void __launch_bounds__(THREADS, 1)
     proj_gemm_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmw, ProjParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Declared 1024-byte aligned (the kernel has no static shared data, so
+  // dynamic shared memory starts on such a boundary; the swizzled tiles need
+  // it).  A misaligned start is counted as a timeout and every thread leaves.
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicAdd(&g_proj_timeouts, 1u);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = p.tiles_m * p.tiles_n;
