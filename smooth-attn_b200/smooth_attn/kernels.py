@@ -1039,12 +1039,20 @@ def _paged_decode_direct(q, k_cache, v_cache, block_table, context_lens, scale, 
     B, H_q, _, D = q.shape
     H_kv = k_cache.shape[1]
     max_blocks_per_seq = block_table.shape[1]
-    q = q.contiguous()
-    k_cache = k_cache.contiguous()
-    v_cache = v_cache.contiguous()
-    block_table = block_table.to(device=q.device, dtype=torch.int32).contiguous()
-    context_lens = context_lens.to(device=q.device, dtype=torch.int32).contiguous()
-    out = torch.empty(B, H_q, D, device=q.device, dtype=torch.bfloat16)
+    # (conversions only when needed: at batch 1 the host's per-call time, not
+    # the kernel, paces back-to-back decode calls)
+    if not q.is_contiguous():
+        q = q.contiguous()
+    if not k_cache.is_contiguous():
+        k_cache = k_cache.contiguous()
+    if not v_cache.is_contiguous():
+        v_cache = v_cache.contiguous()
+    dev = q.device
+    if block_table.dtype is not torch.int32 or block_table.device != dev or not block_table.is_contiguous():
+        block_table = block_table.to(device=dev, dtype=torch.int32).contiguous()
+    if context_lens.dtype is not torch.int32 or context_lens.device != dev or not context_lens.is_contiguous():
+        context_lens = context_lens.to(device=dev, dtype=torch.int32).contiguous()
+    out = torch.empty(B, H_q, D, device=dev, dtype=torch.bfloat16)
     if out.numel() == 0:
         return out
     if max_blocks_per_seq == 0 or k_cache.shape[0] == 0:
