@@ -16,6 +16,11 @@ Timing: CUDA events on the launching stream, W warm-up steps, barrier +
 synchronize around the K timed steps, max over ranks.  Inputs are larger
 than L2 (126 MB), so no flush is needed between steps.
 
+The line's ``e2e`` runs the same workload from pinned host buffers through
+``softplus_norm_causal_host_out`` (both PCIe transfers inside the timed
+region), and ``flash_fwd_bwd`` (last in the line) also reports the
+deterministic backward.
+
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 numpy oracle port, multi-threaded over matrices) on the host cores on a
 bounded sample of the same workload.

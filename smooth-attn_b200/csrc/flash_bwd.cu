@@ -27,6 +27,11 @@
 // The dS tile in shared memory is laid out once (rows = KV, 64-wide query
 // chunks, 128 B swizzle) and read by two MMAs with two descriptors: as a
 // K-major A for dK and as an MN-major A for dQ.
+// D = 128 uses sp2_bwd128_kernel instead (64-row query tiles, double-buffered
+// S^T / dP^T, dQ^T drained by four warps).  The deterministic path
+// (deterministic != 0) runs the key-major kernel without dQ
+// (sp2_bwd_dkv128_kernel for D = 128) and then the query-major
+// sp2_bwd_dq_kernel, which sums every dQ row in one CTA in a fixed order.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
