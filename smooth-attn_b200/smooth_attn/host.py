@@ -104,14 +104,28 @@ def softplus_norm_causal_host_out(out, x, alpha=DEFAULT_FAMILY.alpha, theta=DEFA
 
     # the all-zero columns past every band, on the host (native threads,
     # non-temporal stores), while the GPU works
+    zero_status = []
+
     def zero_tail():
-        _lib.check(lib.sa_host_zero_causal_tail(ctypes.c_void_p(oh.data_ptr()), nmat, L, elem, BAND, 0),
-                   "sa_host_zero_causal_tail")
+        zero_status.append(lib.sa_host_zero_causal_tail(ctypes.c_void_p(oh.data_ptr()), nmat, L, elem, BAND, 0))
 
     zt = threading.Thread(target=zero_tail, daemon=True)
     zt.start()
+    try:
+        _run_slices(lib, dev, xh, oh, nmat, L, elem, nch, per, alpha, theta, power, family)
+    except BaseException:
+        torch.cuda.synchronize(dev)  # no copy still in flight into out when the error surfaces
+        raise
+    finally:
+        zt.join()  # never return (or raise) while the host thread still writes into out
+    _lib.check(zero_status[0] if zero_status else _lib.SA_ERR_ARG, "sa_host_zero_causal_tail")
+    return out
+
+
+def _run_slices(lib, dev, xh, oh, nmat, L, elem, nch, per, alpha, theta, power, family):
+    """Upload bands, run the kernel and download bands, slice by slice."""
     with torch.cuda.device(dev):
-        st = _buffers(dev, nmat, L, x.dtype, nch)
+        st = _buffers(dev, nmat, L, xh.dtype, nch)
         xd, od, s_in, s_out = st["xd"], st["od"], st["s_in"], st["s_out"]
         cur = torch.cuda.current_stream(dev)
         s_in.wait_stream(cur)  # an earlier call's kernels are done with xd
@@ -131,5 +145,3 @@ def softplus_norm_causal_host_out(out, x, alpha=DEFAULT_FAMILY.alpha, theta=DEFA
                        "sa_copy_causal_bands")
         cur.wait_stream(s_out)
         s_out.synchronize()
-    zt.join()
-    return out
